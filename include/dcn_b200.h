@@ -1,0 +1,213 @@
+/*
+ * dcn_b200.h -- C ABI of the B200 (sm_100a) modulated deformable convolution (DCNv2).
+ *
+ * This is the drop-in boundary for the deformable-convolution operator of the
+ * Jasna BasicVSR++ port (ken8303/jasnaMacOS).  Every entry point below replaces
+ * one piece of the reference's Swift/Metal operator; the citation on each names
+ * the reference file and line it stands in for (paths are relative to the
+ * reference project root).
+ *
+ * Conventions
+ *  - Plain C: pointers, sizes, one shape struct.  No CUDA, torch or C++ types.
+ *  - All tensor pointers are DEVICE pointers owned by the caller.  Nothing is
+ *    allocated per call; kernels that need scratch take a caller-provided
+ *    workspace sized by the matching *_workspace_bytes() query.
+ *  - Every launch is asynchronous on the caller's stream (NULL = legacy default
+ *    stream).  A status of DCN_OK means "validated and enqueued".  Errors that
+ *    can only be seen on the device (non-finite output, a device-side pipeline
+ *    timeout) are written to the caller's flag word and/or read back with
+ *    dcn_device_error().
+ *  - Layouts follow the reference (DeformConv.swift:110-132): NCHW input,
+ *    offset [N][2*G*KH*KW][Ho][Wo] with (dy, dx) interleaved per (group, tap),
+ *    mask [N][G*KH*KW][Ho][Wo], output NCHW.  FP32 weights are OIHW; packed
+ *    weights are opaque (sized by dcn_packed_weight_bytes).
+ *  - Thread safety: calls on distinct streams may run concurrently.  The only
+ *    global state is a per-device attribute cache filled once under a mutex and
+ *    the sticky device error word.
+ */
+#ifndef DCN_B200_H
+#define DCN_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define DCN_B200_ABI_VERSION 1
+
+/* Same handle type as cudaStream_t / CUstream, without including CUDA headers. */
+typedef struct CUstream_st *dcn_stream;
+
+/* Mirrors `struct DeformConvShape` (Sources/JasnaMetalPoC/DeformConv.swift:3-20)
+ * field for field and in the same order; `offset_groups` is the deformable-group
+ * count.  The Metal constant block adds `hasMask` (MetalShader.swift:25); every
+ * DCNv2 call in the reference passes a mask, so the mask pointer is simply
+ * required here. */
+typedef struct dcn_shape {
+    int32_t batch;
+    int32_t input_channels;
+    int32_t input_height;
+    int32_t input_width;
+    int32_t output_channels;
+    int32_t output_height;
+    int32_t output_width;
+    int32_t kernel_height;
+    int32_t kernel_width;
+    int32_t pad_height;
+    int32_t pad_width;
+    int32_t stride_height;
+    int32_t stride_width;
+    int32_t dilation_height;
+    int32_t dilation_width;
+    int32_t groups;
+    int32_t offset_groups;
+} dcn_shape;
+
+/* Element counts derived from a shape (DeformConv.swift:22-27). */
+typedef struct dcn_counts {
+    int64_t input;
+    int64_t offset;
+    int64_t mask;
+    int64_t weight;
+    int64_t bias;
+    int64_t output;
+} dcn_counts;
+
+/* Mirrors `enum DeformConvError` (DeformConv.swift:44-73).  The reference's
+ * .metalUnavailable / .shaderResourceMissing become DCN_ERR_NO_DEVICE /
+ * DCN_ERR_UNSUPPORTED; .commandFailed becomes DCN_ERR_LAUNCH (launch error) or
+ * DCN_ERR_DEVICE_TIMEOUT (a bounded device-side wait gave up). */
+typedef enum dcn_status {
+    DCN_OK = 0,
+    DCN_ERR_INVALID_SHAPE = 1,    /* .invalidShape        DeformConv.swift:29-41 */
+    DCN_ERR_INVALID_COUNT = 2,    /* .invalidArrayCount   DeformConv.swift:140-144 */
+    DCN_ERR_NO_DEVICE = 3,        /* .metalUnavailable    MetalRunner.swift:108-110 */
+    DCN_ERR_UNSUPPORTED = 4,      /* .shaderResourceMissing / shape guards MetalRunner.swift:630-713 */
+    DCN_ERR_NONFINITE = 5,        /* .nonFiniteOutput     DeformConv.swift:49,52-55 (the only recoverable one) */
+    DCN_ERR_LAUNCH = 6,           /* .commandFailed       MetalRunner.swift:619-621 */
+    DCN_ERR_INVALID_ARGUMENT = 7, /* NULL pointer / misaligned pointer / short workspace */
+    DCN_ERR_DEVICE_TIMEOUT = 8    /* a device-side bounded wait expired (pipeline error) */
+} dcn_status;
+
+typedef enum dcn_dtype {
+    DCN_DTYPE_F32 = 0,
+    DCN_DTYPE_F16 = 1
+} dcn_dtype;
+
+typedef enum dcn_weight_layout {
+    DCN_WEIGHT_OIHW = 0,      /* [oc][ic/groups][kh][kw]: the direct kernels' layout (MetalShader.swift:118) */
+    DCN_WEIGHT_IC_K_OC = 1    /* [ic][kh*kw][oc]: the reference's prepacked .dcnfp16 layout
+                                 (tools/export_deform_weights.py:47, MetalShader.swift:226-229) */
+} dcn_weight_layout;
+
+/* Bits of the caller's uint32 flag word written by dcn_forward_f16 /
+ * dcn_flag_non_finite_f16 (mirrors flag_non_finite_fp16, MetalShader.swift:454-463). */
+#define DCN_FLAG_NONFINITE 1u
+
+/* Implementation selected by dcn_forward_f16 for a given shape. */
+typedef enum dcn_path {
+    DCN_PATH_DIRECT = 0,      /* CUDA-core direct kernel (any valid shape) */
+    DCN_PATH_FUSED_TC = 1     /* sm_100a fused gather + tcgen05 implicit GEMM */
+} dcn_path;
+
+/* ---- status / shape helpers ------------------------------------------------ */
+
+/* Human-readable text for a status (DeformConvError.description, DeformConv.swift:57-72). */
+const char *dcn_status_string(dcn_status status);
+
+/* 1 for the only recoverable numerical failure, DCN_ERR_NONFINITE
+ * (DeformConvError.isRecoverableNumericalFailure, DeformConv.swift:52-55), else 0. */
+int dcn_status_is_recoverable(dcn_status status);
+
+/* DeformConvShape.validate() (DeformConv.swift:29-41), plus the limits of this
+ * implementation (positive strides/dilations, non-negative pads, 32-bit index
+ * space).  Returns DCN_OK or DCN_ERR_INVALID_SHAPE. */
+dcn_status dcn_shape_validate(const dcn_shape *shape);
+
+/* Element counts of every tensor (DeformConv.swift:22-27). */
+dcn_status dcn_shape_counts(const dcn_shape *shape, dcn_counts *out);
+
+/* Array-count check of DeformConvCPU.require (DeformConv.swift:85-89,140-144).
+ * On DCN_ERR_INVALID_COUNT, *which_out (if non-NULL) gets 0..4 for
+ * input/offset/mask/weight/bias. */
+dcn_status dcn_check_counts(const dcn_shape *shape, int64_t input_count, int64_t offset_count,
+                            int64_t mask_count, int64_t weight_count, int64_t bias_count,
+                            int *which_out);
+
+/* Version of this ABI (DCN_B200_ABI_VERSION). */
+int dcn_abi_version(void);
+
+/* ---- FP32 path ----------------------------------------------------------------
+ * Replaces MetalDeformConv.runFloat32 + deform_conv2d_fp32
+ * (MetalRunner.swift:159-185, MetalShader.swift:76-124).  Any valid shape.
+ * Every output is accumulated in the reference's order (bias, then ic, ky, kx)
+ * with IEEE fp32 multiply/add and no fused multiply-add, so it is bit-identical
+ * to DeformConvCPU.run (DeformConv.swift:98-136). */
+dcn_status dcn_forward_f32(const dcn_shape *shape, const float *input, const float *offset,
+                           const float *mask, const float *weight_oihw, const float *bias,
+                           float *output, dcn_stream stream);
+
+/* ---- FP16 direct path --------------------------------------------------------
+ * Replaces deform_conv2d_fp16 (MetalShader.swift:126-174): FP16 storage, FP32
+ * math in the reference order, one rounding to FP16 at the end.  OIHW FP16
+ * weights, FP16 bias.  Any valid shape.  This is the cross-variant baseline the
+ * reference gates its fast FP16 kernels against (MetalRunner.swift:338-354). */
+dcn_status dcn_forward_f16_direct(const dcn_shape *shape, const void *input, const void *offset,
+                                  const void *mask, const void *weight_oihw, const void *bias,
+                                  void *output, dcn_stream stream);
+
+/* ---- weight prepack ---------------------------------------------------------
+ * Replaces the offline OIHW -> [ic][k][oc] FP16 pack (tools/export_deform_weights.py:47-48,
+ * MetalRunner.swift:235-243).  Produces the opaque packed weight consumed by
+ * dcn_forward_f16: for shapes that take the fused path it is the tcgen05 B
+ * operand (K-major, 128-byte swizzled); otherwise an OIHW FP16 copy.
+ * `weight` is FP32 or FP16 (src_dtype) in OIHW or IC_K_OC layout (src_layout). */
+size_t dcn_packed_weight_bytes(const dcn_shape *shape);
+dcn_status dcn_prepack_weights(const dcn_shape *shape, const void *weight, dcn_dtype src_dtype,
+                               dcn_weight_layout src_layout, void *packed, dcn_stream stream);
+
+/* Which implementation dcn_forward_f16 runs for this shape. */
+dcn_path dcn_forward_f16_path(const dcn_shape *shape);
+
+/* ---- fused FP16 path ----------------------------------------------------------
+ * Replaces deform_conv2d_fp16_jasna_gather + deform_conv2d_fp16_jasna_simdgroup_gemm_fused
+ * + flag_non_finite_fp16 (MetalShader.swift:299-463; host MetalRunner.swift:696-761;
+ * production binding FusedFourPassRecurrenceProbe.swift:609-630).
+ * input/offset/mask/bias/output FP16; packed_weight from dcn_prepack_weights.
+ * `nonfinite_flag` (nullable) gets DCN_FLAG_NONFINITE OR-ed in when any output
+ * is Inf/NaN; the caller zeroes it.  `workspace` must hold
+ * dcn_forward_f16_workspace_bytes(shape) bytes (256-byte aligned); it is
+ * scratch, overwritten by every call. */
+size_t dcn_forward_f16_workspace_bytes(const dcn_shape *shape);
+dcn_status dcn_forward_f16(const dcn_shape *shape, const void *input, const void *offset,
+                           const void *mask, const void *packed_weight, const void *bias,
+                           void *output, uint32_t *nonfinite_flag, void *workspace,
+                           size_t workspace_bytes, dcn_stream stream);
+
+/* ---- non-finite detection -----------------------------------------------------
+ * flag_non_finite_fp16 (MetalShader.swift:454-463): ORs DCN_FLAG_NONFINITE into
+ * *flag if any of `count` FP16 values is Inf or NaN. */
+dcn_status dcn_flag_non_finite_f16(const void *values, int64_t count, uint32_t *flag,
+                                   dcn_stream stream);
+
+/* ---- offset / mask producer ---------------------------------------------------
+ * prepare_dcn_offsets_fp16 (MetalShader.swift:817-839; host MetalRunner.swift:469-508):
+ * raw [432][plane] (288 offset-residue channels then 144 mask logits), flow1 and
+ * flow2 [2][plane] ((x, y) order) -> offset [288][plane] = 10*tanh(raw) + the
+ * flipped flow, mask [144][plane] = sigmoid(raw).  All FP16. */
+dcn_status dcn_prepare_offsets_f16(int64_t plane, const void *raw, const void *flow1,
+                                   const void *flow2, void *offset, void *mask, dcn_stream stream);
+
+/* ---- device error word ----------------------------------------------------------
+ * Every kernel with a bounded device-side wait records a timeout in a sticky
+ * per-device word instead of trapping.  Returns DCN_OK or DCN_ERR_DEVICE_TIMEOUT
+ * for the current device and clears the word (synchronises the device). */
+dcn_status dcn_device_error(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* DCN_B200_H */

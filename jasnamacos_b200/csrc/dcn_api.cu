@@ -1,0 +1,332 @@
+// dcn_api.cu -- the extern "C" boundary declared in include/dcn_b200.h.
+//
+// Validation mirrors DeformConvShape.validate / DeformConvCPU.require
+// (Sources/JasnaMetalPoC/DeformConv.swift:29-41, :140-144) and the Metal
+// runner's shape guards (MetalRunner.swift:630-713), but unsupported shapes
+// return an error instead of the reference kernels' silent early return
+// (MetalShader.swift:192, :254-256).  Launches are asynchronous on the caller's
+// stream; nothing here allocates device memory.
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <cstdlib>
+#include <mutex>
+
+#include "dcn_b200.h"
+#include "dcn_common.cuh"
+
+namespace dcn {
+
+cudaError_t launch_direct_f32(const Params &p, const float *input, const float *offset, const float *mask,
+                              const float *weight, const float *bias, float *output, cudaStream_t stream);
+cudaError_t launch_direct_f16(const Params &p, const __half *input, const __half *offset, const __half *mask,
+                              const __half *weight, const __half *bias, __half *output, cudaStream_t stream);
+cudaError_t launch_prepack_weights(const Params &p, bool fused, int kb, const void *src, dcn_dtype src_dtype,
+                                   int layout, void *dst, cudaStream_t stream);
+cudaError_t launch_flag_non_finite(const __half *values, int64_t count, uint32_t *flag, int sm_count,
+                                   cudaStream_t stream);
+cudaError_t launch_prepare_offsets(int64_t plane, const __half *raw, const __half *flow1, const __half *flow2,
+                                   __half *offset, __half *mask, cudaStream_t stream);
+bool fused_supported(const Params &p);
+int fused_kblocks(const Params &p);
+size_t fused_workspace_bytes(const Params &p);
+cudaError_t fused_prepare_device(uint32_t **err_word);
+cudaError_t launch_fused_f16(const Params &p, const __half *input, const __half *offset, const __half *mask,
+                             const uint8_t *packed_w, const __half *bias, __half *output, uint32_t *flag,
+                             void *workspace, int sm_count, uint32_t *err, cudaStream_t stream);
+
+namespace {
+
+constexpr int kMaxDevices = 64;
+
+struct DeviceInfo {
+    bool ready = false;
+    bool sm100 = false;
+    int sm_count = 0;
+    uint32_t *err_word = nullptr;
+};
+
+std::mutex g_mutex;
+DeviceInfo g_devices[kMaxDevices];
+
+dcn_status from_cuda(cudaError_t e) {
+    if (e == cudaSuccess) return DCN_OK;
+    if (e == cudaErrorNoDevice || e == cudaErrorInsufficientDriver) return DCN_ERR_NO_DEVICE;
+    if (e == cudaErrorNoKernelImageForDevice || e == cudaErrorInvalidDeviceFunction) return DCN_ERR_UNSUPPORTED;
+    return DCN_ERR_LAUNCH;
+}
+
+// Looks up (once per device, under a mutex) the attributes every launch needs.
+dcn_status current_device(DeviceInfo **out) {
+    int dev = -1;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        return from_cuda(e) == DCN_ERR_LAUNCH ? DCN_ERR_NO_DEVICE : from_cuda(e);
+    }
+    if (dev < 0 || dev >= kMaxDevices) return DCN_ERR_NO_DEVICE;
+    std::lock_guard<std::mutex> lock(g_mutex);
+    DeviceInfo &d = g_devices[dev];
+    if (!d.ready) {
+        int major = 0, minor = 0, sms = 0;
+        if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess ||
+            cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev) != cudaSuccess ||
+            cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) {
+            cudaGetLastError();
+            return DCN_ERR_NO_DEVICE;
+        }
+        d.sm100 = (major == 10 && minor == 0);
+        d.sm_count = sms;
+        if (d.sm100) {
+            e = fused_prepare_device(&d.err_word);
+            if (e != cudaSuccess) {
+                cudaGetLastError();
+                return from_cuda(e);
+            }
+        }
+        d.ready = true;
+    }
+    if (!d.sm100) return DCN_ERR_UNSUPPORTED;  // the library carries sm_100a code only
+    *out = &d;
+    return DCN_OK;
+}
+
+bool aligned(const void *p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0; }
+
+// Shape checks beyond DeformConvShape.validate that keep every index the
+// kernels form inside 32 bits per image plane and every position inside int32.
+dcn_status validate(const dcn_shape *s) {
+    if (s == nullptr) return DCN_ERR_INVALID_ARGUMENT;
+    if (!(s->batch > 0 && s->input_channels > 0 && s->output_channels > 0 && s->input_height > 0 &&
+          s->input_width > 0 && s->output_height > 0 && s->output_width > 0 && s->kernel_height > 0 &&
+          s->kernel_width > 0 && s->groups > 0 && s->offset_groups > 0 &&
+          s->input_channels % s->groups == 0 && s->output_channels % s->groups == 0 &&
+          s->input_channels % s->offset_groups == 0))
+        return DCN_ERR_INVALID_SHAPE;
+    const int64_t in_plane = static_cast<int64_t>(s->input_height) * s->input_width;
+    const int64_t out_plane = static_cast<int64_t>(s->output_height) * s->output_width;
+    const int64_t ka = static_cast<int64_t>(s->kernel_height) * s->kernel_width;
+    if (in_plane >= (int64_t{1} << 31) || out_plane >= (int64_t{1} << 31) || ka > 1024)
+        return DCN_ERR_INVALID_SHAPE;
+    // Largest |integer part| of a sampling position: |o*stride| + |pad| + |k*dilation|.
+    auto mag = [](int64_t v) { return v < 0 ? -v : v; };
+    const int64_t ymax = mag(int64_t{s->output_height} * s->stride_height) + mag(s->pad_height) +
+                         mag(int64_t{s->kernel_height} * s->dilation_height);
+    const int64_t xmax = mag(int64_t{s->output_width} * s->stride_width) + mag(s->pad_width) +
+                         mag(int64_t{s->kernel_width} * s->dilation_width);
+    if (ymax >= (int64_t{1} << 30) || xmax >= (int64_t{1} << 30)) return DCN_ERR_INVALID_SHAPE;
+    const int64_t counts[4] = {
+        int64_t{s->batch} * s->input_channels * in_plane,
+        int64_t{s->batch} * 2 * s->offset_groups * ka * out_plane,
+        int64_t{s->batch} * s->output_channels * out_plane,
+        int64_t{s->output_channels} * (s->input_channels / s->groups) * ka,
+    };
+    for (int64_t c : counts)
+        if (c >= (int64_t{1} << 40)) return DCN_ERR_INVALID_SHAPE;
+    return DCN_OK;
+}
+
+}  // namespace
+}  // namespace dcn
+
+using namespace dcn;
+
+extern "C" {
+
+int dcn_abi_version(void) { return DCN_B200_ABI_VERSION; }
+
+const char *dcn_status_string(dcn_status status) {
+    switch (status) {
+    case DCN_OK: return "ok";
+    case DCN_ERR_INVALID_SHAPE: return "Invalid deformable-convolution shape";
+    case DCN_ERR_INVALID_COUNT: return "An array has the wrong number of elements for the shape";
+    case DCN_ERR_NO_DEVICE: return "No CUDA device is available";
+    case DCN_ERR_UNSUPPORTED: return "The shape or device is not supported by this kernel";
+    case DCN_ERR_NONFINITE: return "The deformable convolution produced non-finite output";
+    case DCN_ERR_LAUNCH: return "CUDA launch failed";
+    case DCN_ERR_INVALID_ARGUMENT: return "Invalid argument (null or misaligned pointer, short workspace)";
+    case DCN_ERR_DEVICE_TIMEOUT: return "A device-side wait timed out (pipeline error)";
+    }
+    return "unknown status";
+}
+
+int dcn_status_is_recoverable(dcn_status status) { return status == DCN_ERR_NONFINITE ? 1 : 0; }
+
+dcn_status dcn_shape_validate(const dcn_shape *shape) { return validate(shape); }
+
+dcn_status dcn_shape_counts(const dcn_shape *s, dcn_counts *out) {
+    if (s == nullptr || out == nullptr) return DCN_ERR_INVALID_ARGUMENT;
+    dcn_status st = validate(s);
+    if (st != DCN_OK) return st;
+    const int64_t out_plane = int64_t{s->output_height} * s->output_width;
+    const int64_t ka = int64_t{s->kernel_height} * s->kernel_width;
+    out->input = int64_t{s->batch} * s->input_channels * s->input_height * s->input_width;
+    out->offset = int64_t{s->batch} * 2 * s->offset_groups * ka * out_plane;
+    out->mask = int64_t{s->batch} * s->offset_groups * ka * out_plane;
+    out->weight = int64_t{s->output_channels} * (s->input_channels / s->groups) * ka;
+    out->bias = s->output_channels;
+    out->output = int64_t{s->batch} * s->output_channels * out_plane;
+    return DCN_OK;
+}
+
+dcn_status dcn_check_counts(const dcn_shape *shape, int64_t input_count, int64_t offset_count,
+                            int64_t mask_count, int64_t weight_count, int64_t bias_count, int *which_out) {
+    dcn_counts c;
+    dcn_status st = dcn_shape_counts(shape, &c);
+    if (st != DCN_OK) return st;
+    const int64_t expected[5] = {c.input, c.offset, c.mask, c.weight, c.bias};
+    const int64_t actual[5] = {input_count, offset_count, mask_count, weight_count, bias_count};
+    for (int i = 0; i < 5; ++i) {
+        if (expected[i] != actual[i]) {
+            if (which_out) *which_out = i;
+            return DCN_ERR_INVALID_COUNT;
+        }
+    }
+    return DCN_OK;
+}
+
+dcn_status dcn_forward_f32(const dcn_shape *shape, const float *input, const float *offset, const float *mask,
+                           const float *weight_oihw, const float *bias, float *output, dcn_stream stream) {
+    dcn_status st = validate(shape);
+    if (st != DCN_OK) return st;
+    if (!input || !offset || !mask || !weight_oihw || !bias || !output) return DCN_ERR_INVALID_ARGUMENT;
+    DeviceInfo *dev = nullptr;
+    if ((st = current_device(&dev)) != DCN_OK) return st;
+    return from_cuda(launch_direct_f32(make_params(*shape), input, offset, mask, weight_oihw, bias, output,
+                                       reinterpret_cast<cudaStream_t>(stream)));
+}
+
+dcn_status dcn_forward_f16_direct(const dcn_shape *shape, const void *input, const void *offset,
+                                  const void *mask, const void *weight_oihw, const void *bias, void *output,
+                                  dcn_stream stream) {
+    dcn_status st = validate(shape);
+    if (st != DCN_OK) return st;
+    if (!input || !offset || !mask || !weight_oihw || !bias || !output) return DCN_ERR_INVALID_ARGUMENT;
+    if (!aligned(input, 2) || !aligned(offset, 2) || !aligned(mask, 2) || !aligned(weight_oihw, 2) ||
+        !aligned(bias, 2) || !aligned(output, 2))
+        return DCN_ERR_INVALID_ARGUMENT;
+    DeviceInfo *dev = nullptr;
+    if ((st = current_device(&dev)) != DCN_OK) return st;
+    return from_cuda(launch_direct_f16(
+        make_params(*shape), static_cast<const __half *>(input), static_cast<const __half *>(offset),
+        static_cast<const __half *>(mask), static_cast<const __half *>(weight_oihw),
+        static_cast<const __half *>(bias), static_cast<__half *>(output), reinterpret_cast<cudaStream_t>(stream)));
+}
+
+dcn_path dcn_forward_f16_path(const dcn_shape *shape) {
+    if (validate(shape) != DCN_OK) return DCN_PATH_DIRECT;
+    return fused_supported(make_params(*shape)) ? DCN_PATH_FUSED_TC : DCN_PATH_DIRECT;
+}
+
+size_t dcn_packed_weight_bytes(const dcn_shape *shape) {
+    if (validate(shape) != DCN_OK) return 0;
+    const Params p = make_params(*shape);
+    if (fused_supported(p)) return static_cast<size_t>(fused_kblocks(p)) * 64 * 64 * sizeof(__half);
+    return static_cast<size_t>(p.OC) * p.cpg * p.KA * sizeof(__half);
+}
+
+dcn_status dcn_prepack_weights(const dcn_shape *shape, const void *weight, dcn_dtype src_dtype,
+                               dcn_weight_layout src_layout, void *packed, dcn_stream stream) {
+    dcn_status st = validate(shape);
+    if (st != DCN_OK) return st;
+    if (!weight || !packed) return DCN_ERR_INVALID_ARGUMENT;
+    if (src_dtype != DCN_DTYPE_F32 && src_dtype != DCN_DTYPE_F16) return DCN_ERR_INVALID_ARGUMENT;
+    if (src_layout != DCN_WEIGHT_OIHW && src_layout != DCN_WEIGHT_IC_K_OC) return DCN_ERR_INVALID_ARGUMENT;
+    if (!aligned(weight, src_dtype == DCN_DTYPE_F32 ? 4 : 2) || !aligned(packed, 16))
+        return DCN_ERR_INVALID_ARGUMENT;
+    const Params p = make_params(*shape);
+    // The [ic][k][oc] layout only exists for one convolution group (the reference's packed kernels).
+    if (src_layout == DCN_WEIGHT_IC_K_OC && p.G != 1) return DCN_ERR_UNSUPPORTED;
+    DeviceInfo *dev = nullptr;
+    if ((st = current_device(&dev)) != DCN_OK) return st;
+    const bool fused = fused_supported(p);
+    return from_cuda(launch_prepack_weights(p, fused, fused ? fused_kblocks(p) : 0, weight, src_dtype,
+                                            static_cast<int>(src_layout), packed,
+                                            reinterpret_cast<cudaStream_t>(stream)));
+}
+
+size_t dcn_forward_f16_workspace_bytes(const dcn_shape *shape) {
+    if (validate(shape) != DCN_OK) return 0;
+    const Params p = make_params(*shape);
+    return fused_supported(p) ? fused_workspace_bytes(p) : 0;
+}
+
+dcn_status dcn_forward_f16(const dcn_shape *shape, const void *input, const void *offset, const void *mask,
+                           const void *packed_weight, const void *bias, void *output, uint32_t *nonfinite_flag,
+                           void *workspace, size_t workspace_bytes, dcn_stream stream) {
+    dcn_status st = validate(shape);
+    if (st != DCN_OK) return st;
+    if (!input || !offset || !mask || !packed_weight || !bias || !output) return DCN_ERR_INVALID_ARGUMENT;
+    if (!aligned(input, 2) || !aligned(bias, 2) || !aligned(output, 2) || !aligned(packed_weight, 16) ||
+        (nonfinite_flag && !aligned(nonfinite_flag, 4)))
+        return DCN_ERR_INVALID_ARGUMENT;
+    DeviceInfo *dev = nullptr;
+    if ((st = current_device(&dev)) != DCN_OK) return st;
+    const Params p = make_params(*shape);
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    if (!fused_supported(p)) {
+        if (!aligned(offset, 2) || !aligned(mask, 2)) return DCN_ERR_INVALID_ARGUMENT;
+        cudaError_t e = launch_direct_f16(p, static_cast<const __half *>(input),
+                                          static_cast<const __half *>(offset), static_cast<const __half *>(mask),
+                                          static_cast<const __half *>(packed_weight),
+                                          static_cast<const __half *>(bias), static_cast<__half *>(output), s);
+        if (e == cudaSuccess && nonfinite_flag)
+            e = launch_flag_non_finite(static_cast<const __half *>(output),
+                                       static_cast<int64_t>(p.N) * p.OC * p.out_plane, nonfinite_flag,
+                                       dev->sm_count, s);
+        return from_cuda(e);
+    }
+    // Fused path: offsets/masks are read by TMA (16-byte aligned rows), the
+    // regrouped input by 16-byte loads.
+    if (!aligned(offset, 16) || !aligned(mask, 16)) return DCN_ERR_INVALID_ARGUMENT;
+    if (!workspace || !aligned(workspace, 256) || workspace_bytes < fused_workspace_bytes(p))
+        return DCN_ERR_INVALID_ARGUMENT;
+    return from_cuda(launch_fused_f16(p, static_cast<const __half *>(input), static_cast<const __half *>(offset),
+                                      static_cast<const __half *>(mask),
+                                      static_cast<const uint8_t *>(packed_weight), static_cast<const __half *>(bias),
+                                      static_cast<__half *>(output), nonfinite_flag, workspace, dev->sm_count,
+                                      dev->err_word, s));
+}
+
+dcn_status dcn_flag_non_finite_f16(const void *values, int64_t count, uint32_t *flag, dcn_stream stream) {
+    if (!values || !flag || count <= 0 || !aligned(values, 2) || !aligned(flag, 4)) return DCN_ERR_INVALID_ARGUMENT;
+    DeviceInfo *dev = nullptr;
+    dcn_status st = current_device(&dev);
+    if (st != DCN_OK) return st;
+    return from_cuda(launch_flag_non_finite(static_cast<const __half *>(values), count, flag, dev->sm_count,
+                                            reinterpret_cast<cudaStream_t>(stream)));
+}
+
+dcn_status dcn_prepare_offsets_f16(int64_t plane, const void *raw, const void *flow1, const void *flow2,
+                                   void *offset, void *mask, dcn_stream stream) {
+    if (plane <= 0 || plane >= (int64_t{1} << 31) / 432) return DCN_ERR_INVALID_SHAPE;
+    if (!raw || !flow1 || !flow2 || !offset || !mask) return DCN_ERR_INVALID_ARGUMENT;
+    if (!aligned(raw, 2) || !aligned(flow1, 2) || !aligned(flow2, 2) || !aligned(offset, 2) || !aligned(mask, 2))
+        return DCN_ERR_INVALID_ARGUMENT;
+    DeviceInfo *dev = nullptr;
+    dcn_status st = current_device(&dev);
+    if (st != DCN_OK) return st;
+    return from_cuda(launch_prepare_offsets(plane, static_cast<const __half *>(raw),
+                                            static_cast<const __half *>(flow1), static_cast<const __half *>(flow2),
+                                            static_cast<__half *>(offset), static_cast<__half *>(mask),
+                                            reinterpret_cast<cudaStream_t>(stream)));
+}
+
+dcn_status dcn_device_error(void) {
+    DeviceInfo *dev = nullptr;
+    dcn_status st = current_device(&dev);
+    if (st != DCN_OK) return st;
+    cudaError_t e = cudaDeviceSynchronize();
+    if (e != cudaSuccess) return from_cuda(e);
+    uint32_t word = 0;
+    e = cudaMemcpy(&word, dev->err_word, sizeof(word), cudaMemcpyDeviceToHost);
+    if (e != cudaSuccess) return from_cuda(e);
+    if (word != 0) {
+        const uint32_t zero = 0;
+        cudaMemcpy(dev->err_word, &zero, sizeof(zero), cudaMemcpyHostToDevice);
+        return DCN_ERR_DEVICE_TIMEOUT;
+    }
+    return DCN_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,69 @@
+// dcn_aux.cu -- the two small kernels around the DCNv2 operator.
+//
+//  * non-finite flag: flag_non_finite_fp16 (Sources/JasnaMetalPoC/MetalShader.swift:454-463).
+//    The fused kernel folds this check into its epilogue; this standalone form
+//    serves the direct path and callers that check other tensors.  One atomic
+//    per warp that saw an Inf/NaN instead of one per element.
+//  * offset/mask producer: prepare_dcn_offsets_fp16 (MetalShader.swift:817-839):
+//    offset = 10*tanh(raw) + flipped flow, mask = sigmoid(raw).
+#include <cuda_fp16.h>
+
+#include "dcn_common.cuh"
+
+namespace dcn {
+
+namespace {
+
+__global__ void flag_non_finite_kernel(const __half *__restrict__ values, int64_t count,
+                                       uint32_t *__restrict__ flag) {
+    bool bad = false;
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < count;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const __half h = values[i];
+        bad |= __hisinf(h) != 0 || __hisnan(h);
+    }
+    if (__any_sync(0xffffffffu, bad) && (threadIdx.x % 32) == 0) atomicOr(flag, DCN_FLAG_NONFINITE);
+}
+
+// One thread per (channel, spatial) of the 432-channel raw tensor.
+__global__ void prepare_offsets_kernel(int64_t plane, const __half *__restrict__ raw,
+                                       const __half *__restrict__ flow1, const __half *__restrict__ flow2,
+                                       __half *__restrict__ offset, __half *__restrict__ mask) {
+    const int64_t gid = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (gid >= 432 * plane) return;
+    const int64_t channel = gid / plane;
+    const int64_t spatial = gid % plane;
+    const float v = __half2float(raw[gid]);
+    if (channel < 288) {
+        const int64_t local = channel % 144;
+        const __half *flow = channel < 144 ? flow1 : flow2;
+        // The flow is stored (x, y); offsets are interleaved (dy, dx), so even channels take row 1.
+        const int64_t flow_channel = (local & 1) == 0 ? 1 : 0;
+        const float residue = 10.0f * tanhf(v);
+        offset[gid] = __float2half_rn(residue + __half2float(flow[flow_channel * plane + spatial]));
+    } else {
+        mask[(channel - 288) * plane + spatial] = __float2half_rn(1.0f / (1.0f + expf(-v)));
+    }
+}
+
+}  // namespace
+
+cudaError_t launch_flag_non_finite(const __half *values, int64_t count, uint32_t *flag, int sm_count,
+                                   cudaStream_t stream) {
+    int64_t blocks = (count + 255) / 256;
+    const int64_t cap = static_cast<int64_t>(sm_count) * 8;
+    if (blocks > cap) blocks = cap;
+    if (blocks < 1) blocks = 1;
+    flag_non_finite_kernel<<<static_cast<unsigned>(blocks), 256, 0, stream>>>(values, count, flag);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_prepare_offsets(int64_t plane, const __half *raw, const __half *flow1, const __half *flow2,
+                                   __half *offset, __half *mask, cudaStream_t stream) {
+    const int64_t total = 432 * plane;
+    prepare_offsets_kernel<<<static_cast<unsigned>((total + 255) / 256), 256, 0, stream>>>(
+        plane, raw, flow1, flow2, offset, mask);
+    return cudaGetLastError();
+}
+
+}  // namespace dcn

@@ -1,0 +1,468 @@
+"""Host-side mirror of the reference's deformable-convolution operator.
+
+Mirrors, name for name where Python allows:
+  * ``DeformConvShape`` -- ``struct DeformConvShape`` (Sources/JasnaMetalPoC/DeformConv.swift:3-42)
+  * ``DeformConvError`` -- ``enum DeformConvError`` (DeformConv.swift:44-73)
+  * ``CudaDeformConv``  -- ``final class MetalDeformConv`` (MetalRunner.swift:92-388), the
+    operator the Swift host calls: ``run_float32`` (``runFloat32``, :159-185) plus the FP16
+    entry points its production graph binds (gather + GEMM, FusedFourPassRecurrenceProbe.swift:609-630)
+    and ``benchmark_jasna_shape`` (``benchmarkJasnaShape``, :187-388).
+
+Every computation runs in ``libdcn_b200.so`` through its C ABI; PyTorch only provides
+device memory, streams and events.  There is no CPU fallback: without the library or a
+CUDA device the operator raises.
+"""
+
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass, fields
+
+import numpy as np
+
+from . import _native
+from .benchmark_statistics import BenchmarkStatistics
+
+
+# ----------------------------------------------------------------------------- errors
+
+
+class DeformConvError(Exception):
+    """Base of the operator's errors (DeformConv.swift:44-73)."""
+
+    status = _native.DCN_ERR_LAUNCH
+
+    @property
+    def is_recoverable_numerical_failure(self) -> bool:
+        """Only non-finite output is recoverable (DeformConv.swift:52-55)."""
+        return False
+
+
+class InvalidShape(DeformConvError):
+    status = _native.DCN_ERR_INVALID_SHAPE
+
+    def __init__(self, message: str = "Invalid deformable-convolution shape"):
+        super().__init__(message)
+
+
+class InvalidArrayCount(DeformConvError):
+    status = _native.DCN_ERR_INVALID_COUNT
+
+    def __init__(self, name: str, expected: int, actual: int):
+        self.name, self.expected, self.actual = name, expected, actual
+        super().__init__(f"{name} has {actual} elements; expected {expected}")
+
+
+class DeviceUnavailable(DeformConvError):
+    """The reference's `.metalUnavailable`: no usable CUDA device."""
+
+    status = _native.DCN_ERR_NO_DEVICE
+
+    def __init__(self, message: str = "No CUDA device is available"):
+        super().__init__(message)
+
+
+class Unsupported(DeformConvError):
+    """The reference's `.shaderResourceMissing` / shape guards: no kernel for this case."""
+
+    status = _native.DCN_ERR_UNSUPPORTED
+
+
+class NonFiniteOutput(DeformConvError):
+    status = _native.DCN_ERR_NONFINITE
+
+    def __init__(self, message: str):
+        super().__init__(f"CUDA DCNv2 produced non-finite output: {message}")
+
+    @property
+    def is_recoverable_numerical_failure(self) -> bool:
+        return True
+
+
+class CommandFailed(DeformConvError):
+    status = _native.DCN_ERR_LAUNCH
+
+    def __init__(self, message: str):
+        super().__init__(f"CUDA command failed: {message}")
+
+
+class InvalidArgument(DeformConvError):
+    status = _native.DCN_ERR_INVALID_ARGUMENT
+
+
+class DeviceTimeout(DeformConvError):
+    status = _native.DCN_ERR_DEVICE_TIMEOUT
+
+
+def raise_for_status(status: int, context: str = "") -> None:
+    """Maps a dcn_status to the matching exception (no-op for DCN_OK)."""
+    if status == _native.DCN_OK:
+        return
+    text = _native.status_string(status)
+    msg = f"{context}: {text}" if context else text
+    if status == _native.DCN_ERR_INVALID_SHAPE:
+        raise InvalidShape(msg)
+    if status == _native.DCN_ERR_NO_DEVICE:
+        raise DeviceUnavailable(msg)
+    if status == _native.DCN_ERR_UNSUPPORTED:
+        raise Unsupported(msg)
+    if status == _native.DCN_ERR_NONFINITE:
+        raise NonFiniteOutput(msg)
+    if status == _native.DCN_ERR_INVALID_ARGUMENT:
+        raise InvalidArgument(msg)
+    if status == _native.DCN_ERR_DEVICE_TIMEOUT:
+        raise DeviceTimeout(msg)
+    if status == _native.DCN_ERR_INVALID_COUNT:
+        raise DeformConvError(msg)
+    raise CommandFailed(msg)
+
+
+# ----------------------------------------------------------------------------- shape
+
+
+@dataclass(frozen=True)
+class DeformConvShape:
+    """`struct DeformConvShape` (DeformConv.swift:3-42), same fields in the same order."""
+
+    batch: int
+    input_channels: int
+    input_height: int
+    input_width: int
+    output_channels: int
+    output_height: int
+    output_width: int
+    kernel_height: int
+    kernel_width: int
+    pad_height: int
+    pad_width: int
+    stride_height: int
+    stride_width: int
+    dilation_height: int
+    dilation_width: int
+    groups: int
+    offset_groups: int
+
+    # Derived counts (DeformConv.swift:22-27).
+    @property
+    def input_count(self) -> int:
+        return self.batch * self.input_channels * self.input_height * self.input_width
+
+    @property
+    def output_count(self) -> int:
+        return self.batch * self.output_channels * self.output_height * self.output_width
+
+    @property
+    def kernel_area(self) -> int:
+        return self.kernel_height * self.kernel_width
+
+    @property
+    def offset_count(self) -> int:
+        return self.batch * 2 * self.offset_groups * self.kernel_area * self.output_height * self.output_width
+
+    @property
+    def mask_count(self) -> int:
+        return self.batch * self.offset_groups * self.kernel_area * self.output_height * self.output_width
+
+    @property
+    def weight_count(self) -> int:
+        return self.output_channels * (self.input_channels // self.groups) * self.kernel_area
+
+    @property
+    def output_pixels(self) -> int:
+        return self.batch * self.output_height * self.output_width
+
+    def validate(self) -> None:
+        """DeformConvShape.validate (DeformConv.swift:29-41), plus this build's 32-bit index limits."""
+        c = self.to_c()
+        raise_for_status(_native.load().dcn_shape_validate(ctypes.byref(c)))
+
+    def validate_reference(self) -> bool:
+        """The reference's own predicate only (no library needed)."""
+        s = self
+        return (
+            s.batch > 0 and s.input_channels > 0 and s.output_channels > 0
+            and s.input_height > 0 and s.input_width > 0
+            and s.output_height > 0 and s.output_width > 0
+            and s.kernel_height > 0 and s.kernel_width > 0
+            and s.groups > 0 and s.offset_groups > 0
+            and s.input_channels % s.groups == 0
+            and s.output_channels % s.groups == 0
+            and s.input_channels % s.offset_groups == 0
+        )
+
+    def to_c(self) -> _native.DcnShape:
+        return _native.DcnShape(*[getattr(self, f.name) for f in fields(self)])
+
+    def with_batch(self, batch: int) -> "DeformConvShape":
+        values = {f.name: getattr(self, f.name) for f in fields(self)}
+        values["batch"] = batch
+        return DeformConvShape(**values)
+
+    def as_tuple(self) -> tuple[int, ...]:
+        return tuple(getattr(self, f.name) for f in fields(self))
+
+    @classmethod
+    def jasna_propagation(cls, batch: int = 1, height: int = 64, width: int = 64) -> "DeformConvShape":
+        """BasicVSR++ propagation alignment: 128 -> 64 channels, 3x3, pad 1, 16 deformable
+        groups (PropagationDeformConvShape, MetalMLProbe.swift:47-66; MetalRunner.swift:191-209)."""
+        return cls(batch, 128, height, width, 64, height, width, 3, 3, 1, 1, 1, 1, 1, 1, 1, 16)
+
+
+def check_counts(shape: DeformConvShape, input, offset, mask, weight, bias) -> None:
+    """DeformConvCPU.require (DeformConv.swift:85-89, :140-144) for array-likes."""
+    names = ("input", "offset", "mask", "weight", "bias")
+    expected = (shape.input_count, shape.offset_count, shape.mask_count, shape.weight_count,
+                shape.output_channels)
+    for name, arr, want in zip(names, (input, offset, mask, weight, bias), expected):
+        n = int(np.prod(arr.shape)) if hasattr(arr, "shape") else len(arr)
+        if n != want:
+            raise InvalidArrayCount(name, want, n)
+
+
+# ----------------------------------------------------------------------------- operator
+
+
+def _torch():
+    import torch
+
+    return torch
+
+
+def _ptr(t) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+def _stream_handle(stream) -> int | None:
+    torch = _torch()
+    s = stream if stream is not None else torch.cuda.current_stream()
+    return s.cuda_stream or None
+
+
+class CudaDeformConv:
+    """The CUDA counterpart of `MetalDeformConv` (MetalRunner.swift:92-388).
+
+    Device-tensor methods (``forward_*``, ``prepack``, ``flag_non_finite``,
+    ``prepare_offsets``) take CUDA tensors and enqueue work on the current (or
+    given) stream; host methods (``run_float32``, ``run_float16``) take numpy
+    arrays, copy them to the device, run, synchronise and return numpy arrays,
+    like the reference's synchronous ``runFloat32``.
+    """
+
+    def __init__(self, device: int | None = None):
+        torch = _torch()
+        self.lib = _native.load()
+        if not torch.cuda.is_available():
+            raise DeviceUnavailable()
+        self.device = torch.device("cuda", torch.cuda.current_device() if device is None else device)
+
+    # -- queries ---------------------------------------------------------------
+    def path(self, shape: DeformConvShape) -> int:
+        return self.lib.dcn_forward_f16_path(ctypes.byref(shape.to_c()))
+
+    def packed_weight_bytes(self, shape: DeformConvShape) -> int:
+        return int(self.lib.dcn_packed_weight_bytes(ctypes.byref(shape.to_c())))
+
+    def workspace_bytes(self, shape: DeformConvShape) -> int:
+        return int(self.lib.dcn_forward_f16_workspace_bytes(ctypes.byref(shape.to_c())))
+
+    # -- device-tensor API -----------------------------------------------------
+    def _check_device(self, *tensors) -> None:
+        for t in tensors:
+            if t is not None and (not t.is_cuda or not t.is_contiguous()):
+                raise InvalidArgument("tensors must be contiguous CUDA tensors")
+
+    def forward_f32(self, shape, input, offset, mask, weight, bias, out=None, stream=None):
+        """deform_conv2d_fp32 (MetalShader.swift:76-124) on device tensors; bit-exact with the CPU reference."""
+        torch = _torch()
+        check_counts(shape, input, offset, mask, weight, bias)
+        if out is None:
+            out = torch.empty(shape.output_count, dtype=torch.float32, device=input.device)
+        self._check_device(input, offset, mask, weight, bias, out)
+        with torch.cuda.device(input.device):
+            st = self.lib.dcn_forward_f32(
+                ctypes.byref(shape.to_c()), _ptr(input), _ptr(offset), _ptr(mask), _ptr(weight), _ptr(bias),
+                _ptr(out), _stream_handle(stream))
+        raise_for_status(st, "dcn_forward_f32")
+        return out
+
+    def forward_f16_direct(self, shape, input, offset, mask, weight_oihw, bias, out=None, stream=None):
+        """deform_conv2d_fp16 (MetalShader.swift:126-174): FP16 storage, FP32 math, OIHW weights."""
+        torch = _torch()
+        check_counts(shape, input, offset, mask, weight_oihw, bias)
+        if out is None:
+            out = torch.empty(shape.output_count, dtype=torch.float16, device=input.device)
+        self._check_device(input, offset, mask, weight_oihw, bias, out)
+        with torch.cuda.device(input.device):
+            st = self.lib.dcn_forward_f16_direct(
+                ctypes.byref(shape.to_c()), _ptr(input), _ptr(offset), _ptr(mask), _ptr(weight_oihw),
+                _ptr(bias), _ptr(out), _stream_handle(stream))
+        raise_for_status(st, "dcn_forward_f16_direct")
+        return out
+
+    def prepack(self, shape, weight, layout: int = _native.DCN_WEIGHT_OIHW, stream=None):
+        """Weight prepack kernel: FP32/FP16 OIHW or [ic][k][oc] -> the opaque packed FP16 weight."""
+        torch = _torch()
+        if int(np.prod(weight.shape)) != shape.weight_count:
+            raise InvalidArrayCount("weight", shape.weight_count, int(np.prod(weight.shape)))
+        dtype = {torch.float32: _native.DCN_DTYPE_F32, torch.float16: _native.DCN_DTYPE_F16}.get(weight.dtype)
+        if dtype is None:
+            raise InvalidArgument("weight must be float32 or float16")
+        nbytes = self.packed_weight_bytes(shape)
+        if nbytes == 0:
+            raise InvalidShape()
+        packed = torch.empty(nbytes, dtype=torch.uint8, device=weight.device)
+        self._check_device(weight, packed)
+        with torch.cuda.device(weight.device):
+            st = self.lib.dcn_prepack_weights(ctypes.byref(shape.to_c()), _ptr(weight), dtype, layout,
+                                              _ptr(packed), _stream_handle(stream))
+        raise_for_status(st, "dcn_prepack_weights")
+        return packed
+
+    def forward_f16(self, shape, input, offset, mask, packed_weight, bias, out=None, flag=None,
+                    workspace=None, stream=None):
+        """Fused FP16 DCNv2 (gather + tcgen05 GEMM + epilogue); replaces the reference's
+        gather + SIMD-group GEMM + non-finite-flag passes (MetalShader.swift:299-463)."""
+        torch = _torch()
+        for name, arr, want in (("input", input, shape.input_count), ("offset", offset, shape.offset_count),
+                                ("mask", mask, shape.mask_count), ("bias", bias, shape.output_channels)):
+            if arr.numel() != want:
+                raise InvalidArrayCount(name, want, arr.numel())
+        if out is None:
+            out = torch.empty(shape.output_count, dtype=torch.float16, device=input.device)
+        ws_bytes = self.workspace_bytes(shape)
+        if workspace is None and ws_bytes > 0:
+            workspace = torch.empty(ws_bytes, dtype=torch.uint8, device=input.device)
+        self._check_device(input, offset, mask, packed_weight, bias, out, flag, workspace)
+        with torch.cuda.device(input.device):
+            st = self.lib.dcn_forward_f16(
+                ctypes.byref(shape.to_c()), _ptr(input), _ptr(offset), _ptr(mask), _ptr(packed_weight),
+                _ptr(bias), _ptr(out), _ptr(flag), _ptr(workspace),
+                0 if workspace is None else workspace.numel() * workspace.element_size(), _stream_handle(stream))
+        raise_for_status(st, "dcn_forward_f16")
+        return out
+
+    def flag_non_finite(self, values, flag, stream=None):
+        """flag_non_finite_fp16 (MetalShader.swift:454-463)."""
+        self._check_device(values, flag)
+        st = self.lib.dcn_flag_non_finite_f16(_ptr(values), values.numel(), _ptr(flag), _stream_handle(stream))
+        raise_for_status(st, "dcn_flag_non_finite_f16")
+        return flag
+
+    def prepare_offsets(self, plane: int, raw, flow1, flow2, offset=None, mask=None, stream=None):
+        """prepare_dcn_offsets_fp16 (MetalShader.swift:817-839; MetalRunner.swift:469-508)."""
+        torch = _torch()
+        if raw.numel() != 432 * plane or flow1.numel() != 2 * plane or flow2.numel() != 2 * plane:
+            raise InvalidShape()
+        if offset is None:
+            offset = torch.empty(288 * plane, dtype=torch.float16, device=raw.device)
+        if mask is None:
+            mask = torch.empty(144 * plane, dtype=torch.float16, device=raw.device)
+        self._check_device(raw, flow1, flow2, offset, mask)
+        st = self.lib.dcn_prepare_offsets_f16(plane, _ptr(raw), _ptr(flow1), _ptr(flow2), _ptr(offset),
+                                              _ptr(mask), _stream_handle(stream))
+        raise_for_status(st, "dcn_prepare_offsets_f16")
+        return offset, mask
+
+    def device_error(self) -> None:
+        """Raises DeviceTimeout if a kernel's bounded device-side wait expired since the last check."""
+        raise_for_status(self.lib.dcn_device_error(), "device error word")
+
+    # -- host-array API (synchronous, like the reference) -------------------------
+    def run_float32(self, shape: DeformConvShape, input, offset, mask, weight, bias) -> np.ndarray:
+        """`runFloat32(shape:input:offset:mask:weight:bias:)` (MetalRunner.swift:159-185)."""
+        torch = _torch()
+        shape.validate()
+        check_counts(shape, input, offset, mask, weight, bias)
+        dev = self.device
+
+        def up(a):
+            return torch.from_numpy(np.ascontiguousarray(a, dtype=np.float32).reshape(-1)).to(dev)
+
+        out = self.forward_f32(shape, up(input), up(offset), up(mask), up(weight), up(bias))
+        torch.cuda.synchronize(dev)
+        self.device_error()
+        return out.cpu().numpy()
+
+    def run_float16(self, shape: DeformConvShape, input, offset, mask, weight, bias,
+                    weight_layout: int = _native.DCN_WEIGHT_OIHW) -> np.ndarray:
+        """FP16 operator on host arrays: prepack + fused (or direct) kernel + non-finite check.
+        Raises NonFiniteOutput (the only recoverable error) if any output is Inf/NaN."""
+        torch = _torch()
+        shape.validate()
+        check_counts(shape, input, offset, mask, weight, bias)
+        dev = self.device
+
+        def up(a):
+            return torch.from_numpy(np.ascontiguousarray(a, dtype=np.float16).reshape(-1)).to(dev)
+
+        packed = self.prepack(shape, up(weight), weight_layout)
+        flag = torch.zeros(1, dtype=torch.int32, device=dev)
+        out = self.forward_f16(shape, up(input), up(offset), up(mask), packed, up(bias), flag=flag)
+        torch.cuda.synchronize(dev)
+        self.device_error()
+        if int(flag.item()) & _native.DCN_FLAG_NONFINITE:
+            raise NonFiniteOutput("Inf/NaN in the DCNv2 output")
+        return out.cpu().numpy()
+
+    # -- benchmark (benchmarkJasnaShape) ----------------------------------------
+    def benchmark_jasna_shape(self, iterations: int = 20, weight_set=None, seed: int = 0x4A41534E41):
+        """`benchmarkJasnaShape` (MetalRunner.swift:187-388): the Jasna propagation shape in FP16,
+        direct kernel vs the fused tensor-core kernel, 2 warm-ups + `iterations` timed runs each
+        (CUDA events), cross-variant gate <= 0.002 (MetalRunner.swift:350-354), checksum of every
+        257th output (:335-337).  Inputs: U(-1,1) input, U(-0.25,0.25) offsets, U(0.25,0.75) mask,
+        U(-0.02,0.02) weight/bias (:210-234), drawn from this package's seeded generator."""
+        from . import synthetic
+
+        torch = _torch()
+        shape = DeformConvShape.jasna_propagation()
+        rng = synthetic.SplitMix64(seed)
+        dev = self.device
+        to16 = lambda a: torch.from_numpy(a.astype(np.float16)).to(dev)  # noqa: E731
+        x = to16(rng.uniform(shape.input_count, -1.0, 1.0))
+        off = to16(rng.uniform(shape.offset_count, -0.25, 0.25))
+        msk = to16(rng.uniform(shape.mask_count, 0.25, 0.75))
+        if weight_set is not None:
+            packed_ickoc, bias_np = weight_set.arrays()
+            w_oihw = to16(np.transpose(packed_ickoc.reshape(128, 9, 64), (2, 0, 1)).reshape(-1))
+            bias = to16(bias_np)
+        else:
+            w_oihw = to16(rng.uniform(shape.weight_count, -0.02, 0.02))
+            bias = to16(rng.uniform(shape.output_channels, -0.02, 0.02))
+        packed = self.prepack(shape, w_oihw)
+        out_direct = torch.empty(shape.output_count, dtype=torch.float16, device=dev)
+        out_fused = torch.empty_like(out_direct)
+        flag = torch.zeros(1, dtype=torch.int32, device=dev)
+        ws = torch.empty(max(self.workspace_bytes(shape), 1), dtype=torch.uint8, device=dev)
+
+        def timed(fn):
+            samples = []
+            for _ in range(2):
+                fn()
+            for _ in range(max(iterations, 1)):
+                a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                a.record()
+                fn()
+                b.record()
+                b.synchronize()
+                samples.append(a.elapsed_time(b))
+            return BenchmarkStatistics.from_samples(samples)
+
+        direct_stats = timed(lambda: self.forward_f16_direct(shape, x, off, msk, w_oihw, bias, out=out_direct))
+        fused_stats = timed(lambda: self.forward_f16(shape, x, off, msk, packed, bias, out=out_fused, flag=flag,
+                                                     workspace=ws))
+        torch.cuda.synchronize(dev)
+        self.device_error()
+        diff = (out_fused.float() - out_direct.float()).abs().max().item()
+        if not diff <= 0.002:
+            raise CommandFailed(f"fused FP16 result differs from the direct kernel by {diff}")
+        if direct_stats is None or fused_stats is None:
+            raise CommandFailed("invalid DCNv2 benchmark samples")
+        checksum = float(out_fused[::257].double().sum().item())
+        return {
+            "direct": direct_stats,
+            "fused": fused_stats,
+            "iterations": len(fused_stats.samples),
+            "checksum": checksum,
+            "max_difference_from_direct": diff,
+            "nonfinite": bool(int(flag.item()) & _native.DCN_FLAG_NONFINITE),
+        }

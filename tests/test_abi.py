@@ -1,0 +1,99 @@
+"""The C ABI without a GPU: the library loads, exports every symbol include/dcn_b200.h
+declares, and its host-only entry points (validation, counts, sizes, status text) behave.
+No call here launches device work."""
+
+from __future__ import annotations
+
+import ctypes
+import re
+import subprocess
+from pathlib import Path
+
+import pytest
+
+from jasnamacos_b200 import _native
+from jasnamacos_b200.deform_conv import DeformConvShape
+
+REPO = Path(__file__).resolve().parent.parent
+HEADER = REPO / "include" / "dcn_b200.h"
+
+
+def declared_functions() -> list[str]:
+    text = re.sub(r"/\*.*?\*/", "", HEADER.read_text(), flags=re.S)
+    return sorted(set(re.findall(r"\b(dcn_[a-z0-9_]+)\s*\(", text)))
+
+
+@pytest.fixture(scope="module")
+def lib():
+    return _native.load()
+
+
+def test_header_declarations_are_all_exported(lib):
+    names = declared_functions()
+    assert len(names) >= 15
+    exported = subprocess.run(["nm", "-D", "--defined-only", str(_native.LIB_PATH)], capture_output=True,
+                              text=True, check=True).stdout
+    for name in names:
+        assert re.search(rf"\bT {name}$", exported, flags=re.M), f"{name} not exported"
+        getattr(lib, name)
+    assert set(names) == set(_native.PROTOTYPES), "ctypes prototypes and header disagree"
+
+
+def test_library_is_self_contained():
+    deps = subprocess.run(["ldd", str(_native.LIB_PATH)], capture_output=True, text=True).stdout
+    assert "libcudart" not in deps  # runtime linked statically
+
+
+def test_abi_version_and_status_strings(lib):
+    assert lib.dcn_abi_version() == 1
+    for code in range(9):
+        assert lib.dcn_status_string(code)
+    assert lib.dcn_status_is_recoverable(_native.DCN_ERR_NONFINITE) == 1
+    for code in (0, 1, 2, 3, 4, 6, 7, 8):
+        assert lib.dcn_status_is_recoverable(code) == 0
+
+
+def test_shape_validation_and_counts(lib):
+    s = DeformConvShape.jasna_propagation().to_c()
+    assert lib.dcn_shape_validate(ctypes.byref(s)) == _native.DCN_OK
+    c = _native.DcnCounts()
+    assert lib.dcn_shape_counts(ctypes.byref(s), ctypes.byref(c)) == 0
+    assert (c.input, c.offset, c.mask, c.weight, c.bias, c.output) == (
+        524288, 1179648, 589824, 73728, 64, 262144)
+    bad = DeformConvShape(1, 128, 64, 64, 64, 64, 64, 3, 3, 1, 1, 1, 1, 1, 1, 1, 3).to_c()
+    assert lib.dcn_shape_validate(ctypes.byref(bad)) == _native.DCN_ERR_INVALID_SHAPE
+    assert lib.dcn_shape_validate(None) == _native.DCN_ERR_INVALID_ARGUMENT
+
+
+def test_check_counts(lib):
+    s = DeformConvShape(1, 1, 2, 2, 1, 2, 2, 1, 1, 0, 0, 1, 1, 1, 1, 1, 1).to_c()
+    which = ctypes.c_int(-1)
+    assert lib.dcn_check_counts(ctypes.byref(s), 4, 8, 4, 1, 1, ctypes.byref(which)) == 0
+    assert lib.dcn_check_counts(ctypes.byref(s), 4, 8, 3, 1, 1, ctypes.byref(which)) == _native.DCN_ERR_INVALID_COUNT
+    assert which.value == 2
+
+
+def test_path_selection_and_sizes(lib):
+    jasna = DeformConvShape.jasna_propagation().to_c()
+    assert lib.dcn_forward_f16_path(ctypes.byref(jasna)) == _native.DCN_PATH_FUSED_TC
+    assert lib.dcn_packed_weight_bytes(ctypes.byref(jasna)) == 18 * 8192
+    assert lib.dcn_forward_f16_workspace_bytes(ctypes.byref(jasna)) == 128 * 64 * 64 * 2
+    # 32 output channels -> direct path, OIHW FP16 packed weight, no workspace.
+    other = DeformConvShape(1, 128, 64, 64, 32, 64, 64, 3, 3, 1, 1, 1, 1, 1, 1, 1, 16).to_c()
+    assert lib.dcn_forward_f16_path(ctypes.byref(other)) == _native.DCN_PATH_DIRECT
+    assert lib.dcn_packed_weight_bytes(ctypes.byref(other)) == 32 * 128 * 9 * 2
+    assert lib.dcn_forward_f16_workspace_bytes(ctypes.byref(other)) == 0
+    # 5x5 output plane (25 px, not a multiple of 8) -> direct path.
+    odd = DeformConvShape.jasna_propagation(1, 5, 5).to_c()
+    assert lib.dcn_forward_f16_path(ctypes.byref(odd)) == _native.DCN_PATH_DIRECT
+
+
+def test_null_pointers_are_rejected_before_any_device_work(lib):
+    s = DeformConvShape.jasna_propagation().to_c()
+    args = [None] * 6
+    assert lib.dcn_forward_f32(ctypes.byref(s), *args, None) == _native.DCN_ERR_INVALID_ARGUMENT
+    assert lib.dcn_forward_f16_direct(ctypes.byref(s), *args, None) == _native.DCN_ERR_INVALID_ARGUMENT
+    assert lib.dcn_forward_f16(ctypes.byref(s), *args, None, None, 0, None) == _native.DCN_ERR_INVALID_ARGUMENT
+    assert lib.dcn_prepack_weights(ctypes.byref(s), None, 0, 0, None, None) == _native.DCN_ERR_INVALID_ARGUMENT
+    assert lib.dcn_flag_non_finite_f16(None, 4, None, None) == _native.DCN_ERR_INVALID_ARGUMENT
+    assert lib.dcn_prepare_offsets_f16(0, None, None, None, None, None, None) == _native.DCN_ERR_INVALID_SHAPE

@@ -1,0 +1,110 @@
+"""GPU checks of the operator's error contract and helper kernels, through the C ABI:
+non-finite detection (MetalNonFiniteFlagTests.swift, MetalShader.swift:454-463), the offset
+transform (MetalShader.swift:817-839 vs JasnaCLI.swift:177-211), host-side argument
+errors, the device error word and the reference-style benchmark."""
+
+from __future__ import annotations
+
+import ctypes
+import math
+
+import numpy as np
+import pytest
+
+import oracle
+from golden_data import reference_kats
+from jasnamacos_b200 import _native, synthetic
+from jasnamacos_b200.deform_conv import DeformConvShape, InvalidArgument, NonFiniteOutput
+
+pytestmark = pytest.mark.gpu
+
+
+def test_non_finite_flag_reference_cases(cuda_op):
+    import torch
+
+    for values, expected in reference_kats()["non_finite_flag"]["cases"]:
+        vals = torch.tensor([float(v) for v in values], dtype=torch.float16, device="cuda")
+        flag = torch.zeros(1, dtype=torch.int32, device="cuda")
+        cuda_op.flag_non_finite(vals, flag)
+        torch.cuda.synchronize()
+        assert int(flag.item()) == expected, values
+
+
+def test_fused_epilogue_flags_non_finite_output(cuda_op):
+    inp = synthetic.generate(1)
+    x = inp.input.copy()
+    x[1234] = np.inf  # a sample that lands on it turns the output non-finite
+    with pytest.raises(NonFiniteOutput) as e:
+        cuda_op.run_float16(inp.shape, x, inp.offset, inp.mask, inp.weight, inp.bias)
+    assert e.value.is_recoverable_numerical_failure
+    # a finite run of the same operator does not raise
+    cuda_op.run_float16(inp.shape, inp.input, inp.offset, inp.mask, inp.weight, inp.bias)
+
+
+def test_direct_path_flags_non_finite_output(cuda_op):
+    s = DeformConvShape.jasna_propagation(1, 5, 5)  # direct path
+    g = synthetic.SplitMix64(5)
+    arrays = [g.uniform(n, -1, 1) for n in (s.input_count, s.offset_count, s.mask_count, s.weight_count,
+                                              s.output_channels)]
+    arrays[3][0] = 70000.0  # overflows FP16 -> Inf weight
+    with pytest.raises(NonFiniteOutput):
+        cuda_op.run_float16(s, *arrays)
+
+
+def test_offset_transform_reference_cli_case(cuda_op):
+    import torch
+
+    kat = reference_kats()["offset_transform"]
+    plane = kat["plane"]
+    raw, f1, f2 = (np.array(kat[k], np.float32) for k in ("raw", "flow1", "flow2"))
+    off, msk = cuda_op.prepare_offsets(plane, *(torch.from_numpy(a).half().cuda() for a in (raw, f1, f2)))
+    torch.cuda.synchronize()
+    ref_off, ref_msk = oracle.prepare_offsets(plane, raw, f1, f2)
+    err = max(np.abs(off.float().cpu().numpy() - ref_off).max(), np.abs(msk.float().cpu().numpy() - ref_msk).max())
+    assert err < kat["tolerance"]  # JasnaCLI.swift:208
+
+
+def test_misaligned_pointers_are_rejected_on_the_host(cuda_op):
+    import torch
+
+    s = DeformConvShape.jasna_propagation()
+    x = torch.zeros(s.input_count, dtype=torch.float16, device="cuda")
+    off_big = torch.zeros(s.offset_count + 1, dtype=torch.float16, device="cuda")
+    msk = torch.zeros(s.mask_count, dtype=torch.float16, device="cuda")
+    w = torch.zeros(s.weight_count, dtype=torch.float16, device="cuda")
+    b = torch.zeros(64, dtype=torch.float16, device="cuda")
+    packed = cuda_op.prepack(s, w)
+    with pytest.raises(InvalidArgument):
+        cuda_op.forward_f16(s, x, off_big[1:], msk, packed, b)  # offset rows must be 16-byte aligned
+    ws = torch.zeros(cuda_op.workspace_bytes(s) // 2, dtype=torch.uint8, device="cuda")
+    with pytest.raises(InvalidArgument):
+        cuda_op.forward_f16(s, x, off_big[:-1], msk, packed, b, workspace=ws)  # short workspace
+
+
+def test_device_error_word_is_clear(cuda_op):
+    assert cuda_op.lib.dcn_device_error() == _native.DCN_OK
+
+
+def test_benchmark_jasna_shape(cuda_op):
+    r = cuda_op.benchmark_jasna_shape(iterations=5)
+    assert r["max_difference_from_direct"] <= 0.002
+    assert math.isfinite(r["checksum"]) and not r["nonfinite"]
+    assert r["fused"].median > 0 and r["direct"].median > 0
+
+
+def test_stream_ordering_on_a_side_stream(cuda_op):
+    """Work is enqueued on the caller's stream: a side stream gives the same result."""
+    import torch
+
+    inp = synthetic.generate(1)
+    s = inp.shape
+    x, off, msk, w, b = [torch.from_numpy(a).cuda() for a in inp.tensors_f16()]
+    packed = cuda_op.prepack(s, w)
+    base = cuda_op.forward_f16(s, x, off, msk, packed, b)
+    torch.cuda.synchronize()
+    side = torch.cuda.Stream()
+    with torch.cuda.stream(side):
+        out = cuda_op.forward_f16(s, x, off, msk, packed, b, stream=side)
+    side.synchronize()
+    assert torch.equal(base, out)
+    assert ctypes.sizeof(ctypes.c_void_p) == 8
