@@ -1,0 +1,421 @@
+"""DCNv2 benchmark: output Mpixels/s of the fused FP16 B200 operator.
+
+Workload (config 4 of the round's benchmark set): N=2048 FP16 tiles of 128x64x64 -> 64x64x64,
+3x3, pad 1, 16 deformable groups, offsets 10*tanh(N(0,1)) + per-pixel flow U(-16,16), mask
+sigmoid(N(0,1)); the 2048 tiles are sharded evenly over the GPUs (total work fixed, so
+"scaling": "strong"), no data-path collective.  Inputs are synthetic, generated on each GPU
+from a fixed seed.  One step = one pass of the operator (C ABI dcn_forward_f16: input regroup
++ fused gather/tcgen05 kernel) over the rank's shard.  Every step reads > 1 GB of inputs per
+GPU, far more than the 126 MB L2, so no separate L2 flush is needed.
+
+Reported: `value` (inputs resident in HBM, CUDA events on the launching stream, max over
+ranks), `e2e` (the host-buffer API forward_f16_host: pinned host -> device copies, kernels,
+device -> host output and flag read, every step), `roofline` (the fused kernel timed alone,
+algorithmic bytes 1248 B/px), `cpu_baseline` (the literal CPU reference loop on a bounded
+sample of the same tiles, rank 0 at N=1).  `--impl reference` times only that CPU reference
+(the reference implementation of this path is CPU code; its GPU code is Metal).
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+  torchrun --nproc-per-node N bench.py --gpus N ...   (one process per GPU, NCCL)
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+REPO = Path(__file__).resolve().parent
+sys.path.insert(0, str(REPO))
+
+TILES = 2048  # config 4; --tiles selects a smaller case of the same distributions (profiling)
+TILE_H = TILE_W = 64
+BYTES_PER_PX = 256 + 576 + 288 + 128  # input + offset + mask + output, FP16
+FLOPS_PER_PX = 2 * 64 * 1152
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+
+def load_peaks():
+    p = REPO / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return d, "measured"
+    return dict(FALLBACK_PEAKS), "fallback"
+
+
+# ----------------------------------------------------------------------------- clocks
+
+
+class ClockSampler:
+    """nvidia-smi samples every 200 ms during the timed region (clocks and throttle reasons)."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines: list[str] = []
+        self._thread = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+            return
+        self._thread = threading.Thread(target=self._read, daemon=True)
+        self._thread.start()
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self) -> dict:
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+            if self._thread is not None:
+                self._thread.join(timeout=2)
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = float(parts[2])
+            except ValueError:
+                continue
+            for name, val in zip(names, parts[5:9]):
+                if val.lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ----------------------------------------------------------------------------- distributed
+
+
+def dist_setup(gpus: int):
+    import torch
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != gpus and world > 1:
+        raise SystemExit(f"--gpus {gpus} but WORLD_SIZE={world}")
+    pg = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+        pg = dist
+    elif torch.cuda.is_available():
+        torch.cuda.set_device(0)
+    return rank, world, local, pg
+
+
+def max_over_ranks(value: float, pg) -> float:
+    if pg is None:
+        return value
+    import torch
+
+    t = torch.tensor([value], dtype=torch.float64, device="cuda")
+    pg.all_reduce(t, op=pg.ReduceOp.MAX)
+    return float(t.item())
+
+
+def barrier(pg):
+    if pg is not None:
+        pg.barrier()
+
+
+# ----------------------------------------------------------------------------- CPU reference
+
+
+def cpu_reference_sample(target_seconds: float = 12.0, threads: int | None = None, distinct_tiles: int = 16):
+    """The literal CPU reference loop (oracle restatement of DeformConvCPU.run) on a bounded
+    sample of config-4 tiles: one tile per host thread, the same output rows of each tile,
+    row count chosen from a one-row calibration so the sample takes ~target_seconds.
+    Returns (px_per_s, threads, description)."""
+    import numpy as np
+
+    import oracle
+    from jasnamacos_b200 import synthetic
+
+    threads = threads or oracle.host_threads()
+    base = synthetic.generate(4, tiles=range(min(distinct_tiles, threads)))
+    per = base.shape.with_batch(1)
+    k = base.shape.batch
+    idx = [t % k for t in range(threads)]
+
+    def tile_stack(arr, count):
+        a = arr.reshape(k, count)
+        return np.ascontiguousarray(a[idx]).reshape(-1)
+
+    shape = per.with_batch(threads)
+    x = tile_stack(base.input, per.input_count)
+    off = tile_stack(base.offset, per.offset_count)
+    msk = tile_stack(base.mask, per.mask_count)
+    t0 = time.perf_counter()
+    oracle.run_sample(shape, x, off, msk, base.weight, base.bias, (0, 1), threads)
+    one_row = time.perf_counter() - t0
+    rows = int(max(1, min(TILE_H, target_seconds / max(one_row, 1e-3))))
+    t0 = time.perf_counter()
+    oracle.run_sample(shape, x, off, msk, base.weight, base.bias, (0, rows), threads)
+    dt = time.perf_counter() - t0
+    px = threads * rows * TILE_W
+    desc = (f"literal DeformConvCPU.run loop (C restatement, -O2, no FMA contraction), {threads} threads x "
+            f"1 config-4 tile each ({min(distinct_tiles, threads)} distinct tiles), output rows 0..{rows - 1} "
+            f"of each tile = {px} output px in {dt:.2f} s")
+    return px / dt, threads, desc, rows, (shape, x, off, msk, base.weight, base.bias)
+
+
+def run_reference_arm(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    import oracle
+
+    oracle.load()
+    threads = oracle.host_threads()
+    # Calibrate once, then every step runs the same bounded sample.
+    rate, threads, desc, rows, data = cpu_reference_sample(target_seconds=2.0, threads=threads)
+    shape, x, off, msk, w, b = data
+    for _ in range(args.warmup):
+        oracle.run_sample(shape, x, off, msk, w, b, (0, rows), threads)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        oracle.run_sample(shape, x, off, msk, w, b, (0, rows), threads)
+    dt = time.perf_counter() - t0
+    px = threads * rows * TILE_W * args.steps
+    value = px / dt / 1e6
+    line = {
+        "impl": "reference",
+        "metric": "DCNv2 output Mpixels/s (config 4: 2048 FP16 tiles 128x64x64->64, 3x3, 16 deformable groups)",
+        "value": value,
+        "unit": "Mpx/s",
+        "n_gpus": args.gpus,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": dt / args.steps * 1e3,
+        "higher_is_better": True,
+        "scaling": "strong",
+        "vs_baseline": None,
+        "dtype": "f32",
+        "data": "synthetic (seeded config-4 tiles)",
+        "config": {"workload": "config 4: 2048 tiles, 64x64, 128->64 ch, 3x3, 16 deformable groups, flow U(-16,16)",
+                   "sample_per_step": f"{threads} tiles x {rows} output rows"},
+        "cpu_baseline": {"value": value, "unit": "Mpx/s", "cores": threads, "kind": "port",
+                         "sample": desc.split(" in ")[0]},
+        "e2e": {"value": value, "unit": "Mpx/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "gpu_launches": 0,
+        "note": "reference DCNv2 CPU implementation (DeformConv.swift:75-166) as its C restatement; "
+                "the reference's GPU kernels are Metal, unavailable on this box",
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ----------------------------------------------------------------------------- our arm
+
+
+def event_time_ms(fn, iters: int, stream=None) -> float:
+    import torch
+
+    s = stream or torch.cuda.current_stream()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(s)
+    for _ in range(iters):
+        fn()
+    b.record(s)
+    b.synchronize()
+    return a.elapsed_time(b)
+
+
+def run_ours(args):
+    import numpy as np
+    import torch
+
+    from jasnamacos_b200 import synthetic
+    from jasnamacos_b200.deform_conv import CudaDeformConv
+
+    rank, world, local, pg = dist_setup(args.gpus)
+    dev = torch.device("cuda", local)
+    op = CudaDeformConv(local)
+    peaks, peak_kind = load_peaks()
+
+    tiles = args.tiles
+    t_begin = tiles * rank // world
+    t_end = tiles * (rank + 1) // world
+    shape = synthetic.config_shape(4, batch=t_end - t_begin)
+    px_per_step = shape.output_pixels
+    x, off, msk, w, b = synthetic.device_batch(shape, 16.0, seed=1000 + t_begin, device=dev)
+    w16 = torch.from_numpy(w).to(dev).half()
+    b16 = torch.from_numpy(b).to(dev).half()
+    packed = op.prepack(shape, w16)
+    out = torch.empty(shape.output_count, dtype=torch.float16, device=dev)
+    flag = torch.zeros(1, dtype=torch.int32, device=dev)
+    ws = torch.empty(op.workspace_bytes(shape), dtype=torch.uint8, device=dev)
+    torch.cuda.synchronize(dev)
+
+    def step():
+        op.forward_f16(shape, x, off, msk, packed, b16, out=out, flag=flag, workspace=ws)
+
+    # ---- device-resident throughput (the `value`) --------------------------------
+    for _ in range(max(args.warmup, 3)):
+        step()
+    torch.cuda.synchronize(dev)
+    sampler = ClockSampler(local)
+    sampler.start()
+    time.sleep(0.3)
+    barrier(pg)
+    torch.cuda.synchronize(dev)
+    ms = event_time_ms(step, args.steps)
+    torch.cuda.synchronize(dev)
+    barrier(pg)
+    clocks = sampler.stop()
+    ms_max = max_over_ranks(ms, pg)
+    ms_per_step = ms_max / args.steps
+    value = tiles * TILE_H * TILE_W / (ms_per_step * 1e-3) / 1e6  # whole job, Mpx/s
+    op.device_error()
+    nonfinite = int(flag.item())
+
+    # ---- dominant kernel alone, for the roofline ----------------------------------
+    op.regroup_input(shape, x, workspace=ws)
+    fused_ms = event_time_ms(
+        lambda: op.forward_f16_grouped(shape, ws, off, msk, packed, b16, out=out, flag=flag), args.steps) / args.steps
+    regroup_ms = event_time_ms(lambda: op.regroup_input(shape, x, workspace=ws), args.steps) / args.steps
+    torch.cuda.synchronize(dev)
+    achieved_gbs = BYTES_PER_PX * px_per_step / (fused_ms * 1e-3) / 1e9
+    tensor_tflops = FLOPS_PER_PX * px_per_step / (fused_ms * 1e-3) / 1e12
+    traffic = None
+    prof = REPO / "profiles" / "fused_dcn_traffic.json"
+    if prof.exists():
+        d = json.loads(prof.read_text())
+        traffic = d.get("dram_bytes_per_output_px", 0) * px_per_step or None
+
+    # ---- end to end through the host-buffer API ------------------------------------
+    e2e = None
+    if not args.no_e2e:
+        one = shape.with_batch(1)
+        h_x = torch.empty(shape.input_count, dtype=torch.float16, pin_memory=True)
+        h_off = torch.empty(shape.offset_count, dtype=torch.float16, pin_memory=True)
+        h_msk = torch.empty(shape.mask_count, dtype=torch.float16, pin_memory=True)
+        h_out = torch.empty(shape.output_count, dtype=torch.float16, pin_memory=True)
+        h_x.copy_(x)
+        h_off.copy_(off)
+        h_msk.copy_(msk)
+        e2e_step = lambda: op.forward_f16_host(shape, h_x, h_off, h_msk, packed, b16, h_out,  # noqa: E731
+                                               chunk_images=64)
+        for _ in range(2):
+            e2e_step()
+        barrier(pg)
+        torch.cuda.synchronize(dev)
+        e_steps = max(1, min(args.steps, args.e2e_steps))
+        t0 = time.perf_counter()
+        a = torch.cuda.Event(enable_timing=True)
+        bev = torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(e_steps):
+            e2e_step()
+        bev.record()
+        bev.synchronize()
+        e_ms = max_over_ranks(a.elapsed_time(bev), pg) / e_steps
+        op.device_error()
+        dev_out = h_out.to(dev)
+        ok = torch.equal(dev_out, out)
+        mism = int((dev_out != out).sum().item())
+        maxdiff = float((dev_out.float() - out.float()).abs().max().item())
+        e2e = {"value": tiles * TILE_H * TILE_W / (e_ms * 1e-3) / 1e6, "unit": "Mpx/s",
+               "h2d_bytes_per_step": (h_x.numel() + h_off.numel() + h_msk.numel()) * 2,
+               "d2h_bytes_per_step": h_out.numel() * 2 + 4, "ms_per_step": e_ms, "steps": e_steps,
+               "matches_device_resident_output": bool(ok), "mismatched_outputs": mism,
+               "max_abs_diff_vs_device_resident": maxdiff, "per_rank_bytes": True}
+        del h_x, h_off, h_msk, h_out, one
+
+    # ---- CPU baseline (rank 0, one GPU only) ----------------------------------------
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        rate, threads, desc, _, _ = cpu_reference_sample(target_seconds=args.cpu_seconds)
+        cpu = {"value": rate / 1e6, "unit": "Mpx/s", "cores": threads, "kind": "port", "sample": desc}
+
+    if pg is not None:
+        barrier(pg)
+    if rank == 0:
+        line = {
+            "metric": "DCNv2 output Mpixels/s (config 4: 2048 FP16 tiles 128x64x64->64, 3x3, 16 deformable groups)",
+            "value": value,
+            "unit": "Mpx/s",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": max(args.warmup, 3),
+            "ms_per_step": ms_per_step,
+            "higher_is_better": True,
+            "scaling": "strong",
+            "vs_baseline": None,
+            "dtype": "f16",
+            "data": "synthetic (seeded on device: x~N(0,1), offset 10*tanh(N(0,1))+flow U(-16,16), "
+                    "mask sigmoid(N(0,1)), Kaiming-uniform weights)",
+            "config": {"workload": f"config 4: N={tiles} tiles of 128x64x64 -> 64x64x64 FP16, 3x3, pad 1, "
+                                   "16 deformable groups, flow U(-16,16), sharded evenly over the GPUs",
+                       "tiles_per_gpu": t_end - t_begin, "px_per_gpu_step": px_per_step,
+                       "l2": "inputs > L2 every step (>1 GB per GPU per step); no flush needed",
+                       "parallelism": f"tile shards x{world}, no data-path collective"},
+            "roofline": {"bound": "hbm", "achieved": achieved_gbs, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                         "frac": achieved_gbs / peaks["hbm_gbs"], "traffic": traffic,
+                         "peak_source": f"{peak_kind} hbm_gbs", "kernel": "fused_dcn_kernel",
+                         "kernel_ms": fused_ms, "regroup_ms": regroup_ms,
+                         "algorithmic_bytes_per_px": BYTES_PER_PX,
+                         "tensor_tflops": tensor_tflops,
+                         "tensor_frac": tensor_tflops / peaks["bf16_tflops"],
+                         "tensor_peak_source": f"{peak_kind} bf16_tflops (burst)"},
+            "cpu_baseline": cpu,
+            "e2e": e2e,
+            "gpu_launches": 2 * args.steps,
+            "clocks": clocks,
+            "nonfinite_flag": nonfinite,
+        }
+        print(json.dumps(line), flush=True)
+    if pg is not None:
+        pg.destroy_process_group()
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    ap.add_argument("--tiles", type=int, default=TILES, help="total tiles (default: config 4's 2048)")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--e2e-steps", type=int, default=5)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=12.0)
+    args = ap.parse_args()
+    if args.impl == "reference":
+        return run_reference_arm(args)
+    return run_ours(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -122,8 +122,10 @@ const char *dcn_status_string(dcn_status status);
 int dcn_status_is_recoverable(dcn_status status);
 
 /* DeformConvShape.validate() (DeformConv.swift:29-41), plus the limits of this
- * implementation (positive strides/dilations, non-negative pads, 32-bit index
- * space).  Returns DCN_OK or DCN_ERR_INVALID_SHAPE. */
+ * implementation: planes below 2^31 elements, kernel area <= 1024, sampling
+ * positions whose integer part stays below 2^30 in magnitude, tensors below
+ * 2^40 elements.  Strides, pads and dilations may take any value the reference
+ * accepts.  Returns DCN_OK or DCN_ERR_INVALID_SHAPE. */
 dcn_status dcn_shape_validate(const dcn_shape *shape);
 
 /* Element counts of every tensor (DeformConv.swift:22-27). */
@@ -185,6 +187,21 @@ dcn_status dcn_forward_f16(const dcn_shape *shape, const void *input, const void
                            const void *mask, const void *packed_weight, const void *bias,
                            void *output, uint32_t *nonfinite_flag, void *workspace,
                            size_t workspace_bytes, dcn_stream stream);
+
+/* The two launches dcn_forward_f16 makes, for callers that keep their features
+ * channels-last and for timing the fused kernel alone.
+ * dcn_regroup_input_f16: NCHW FP16 input -> "group-blocked channels-last"
+ *   [N][C/8][H][W][8] FP16 in `workspace` (dcn_forward_f16_workspace_bytes bytes),
+ *   so the 8 channels of one deformable group at one position are 16 contiguous bytes.
+ * dcn_forward_f16_grouped: the fused gather + tcgen05 kernel reading such a grouped
+ *   input (16-byte aligned).  Both require dcn_forward_f16_path() == DCN_PATH_FUSED_TC
+ *   and return DCN_ERR_UNSUPPORTED otherwise. */
+dcn_status dcn_regroup_input_f16(const dcn_shape *shape, const void *input, void *workspace,
+                                 size_t workspace_bytes, dcn_stream stream);
+dcn_status dcn_forward_f16_grouped(const dcn_shape *shape, const void *input_grouped,
+                                   const void *offset, const void *mask, const void *packed_weight,
+                                   const void *bias, void *output, uint32_t *nonfinite_flag,
+                                   dcn_stream stream);
 
 /* ---- non-finite detection -----------------------------------------------------
  * flag_non_finite_fp16 (MetalShader.swift:454-463): ORs DCN_FLAG_NONFINITE into

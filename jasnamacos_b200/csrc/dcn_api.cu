@@ -31,9 +31,10 @@ bool fused_supported(const Params &p);
 int fused_kblocks(const Params &p);
 size_t fused_workspace_bytes(const Params &p);
 cudaError_t fused_prepare_device(uint32_t **err_word);
-cudaError_t launch_fused_f16(const Params &p, const __half *input, const __half *offset, const __half *mask,
-                             const uint8_t *packed_w, const __half *bias, __half *output, uint32_t *flag,
-                             void *workspace, int sm_count, uint32_t *err, cudaStream_t stream);
+cudaError_t launch_regroup_c8(const Params &p, const __half *input, void *workspace, cudaStream_t stream);
+cudaError_t launch_fused_grouped(const Params &p, const void *input_c8, const __half *offset, const __half *mask,
+                                 const uint8_t *packed_w, const __half *bias, __half *output, uint32_t *flag,
+                                 int sm_count, uint32_t *err, cudaStream_t stream);
 
 namespace {
 
@@ -281,11 +282,49 @@ dcn_status dcn_forward_f16(const dcn_shape *shape, const void *input, const void
     if (!aligned(offset, 16) || !aligned(mask, 16)) return DCN_ERR_INVALID_ARGUMENT;
     if (!workspace || !aligned(workspace, 256) || workspace_bytes < fused_workspace_bytes(p))
         return DCN_ERR_INVALID_ARGUMENT;
-    return from_cuda(launch_fused_f16(p, static_cast<const __half *>(input), static_cast<const __half *>(offset),
-                                      static_cast<const __half *>(mask),
-                                      static_cast<const uint8_t *>(packed_weight), static_cast<const __half *>(bias),
-                                      static_cast<__half *>(output), nonfinite_flag, workspace, dev->sm_count,
-                                      dev->err_word, s));
+    cudaError_t e = launch_regroup_c8(p, static_cast<const __half *>(input), workspace, s);
+    if (e != cudaSuccess) return from_cuda(e);
+    return from_cuda(launch_fused_grouped(p, workspace, static_cast<const __half *>(offset),
+                                          static_cast<const __half *>(mask),
+                                          static_cast<const uint8_t *>(packed_weight),
+                                          static_cast<const __half *>(bias), static_cast<__half *>(output),
+                                          nonfinite_flag, dev->sm_count, dev->err_word, s));
+}
+
+dcn_status dcn_regroup_input_f16(const dcn_shape *shape, const void *input, void *workspace,
+                                 size_t workspace_bytes, dcn_stream stream) {
+    dcn_status st = validate(shape);
+    if (st != DCN_OK) return st;
+    const Params p = make_params(*shape);
+    if (!fused_supported(p)) return DCN_ERR_UNSUPPORTED;
+    if (!input || !workspace || !aligned(input, 2) || !aligned(workspace, 256) ||
+        workspace_bytes < fused_workspace_bytes(p))
+        return DCN_ERR_INVALID_ARGUMENT;
+    DeviceInfo *dev = nullptr;
+    if ((st = current_device(&dev)) != DCN_OK) return st;
+    return from_cuda(launch_regroup_c8(p, static_cast<const __half *>(input), workspace,
+                                       reinterpret_cast<cudaStream_t>(stream)));
+}
+
+dcn_status dcn_forward_f16_grouped(const dcn_shape *shape, const void *input_grouped, const void *offset,
+                                   const void *mask, const void *packed_weight, const void *bias, void *output,
+                                   uint32_t *nonfinite_flag, dcn_stream stream) {
+    dcn_status st = validate(shape);
+    if (st != DCN_OK) return st;
+    const Params p = make_params(*shape);
+    if (!fused_supported(p)) return DCN_ERR_UNSUPPORTED;
+    if (!input_grouped || !offset || !mask || !packed_weight || !bias || !output) return DCN_ERR_INVALID_ARGUMENT;
+    if (!aligned(input_grouped, 16) || !aligned(offset, 16) || !aligned(mask, 16) || !aligned(packed_weight, 16) ||
+        !aligned(bias, 2) || !aligned(output, 2) || (nonfinite_flag && !aligned(nonfinite_flag, 4)))
+        return DCN_ERR_INVALID_ARGUMENT;
+    DeviceInfo *dev = nullptr;
+    if ((st = current_device(&dev)) != DCN_OK) return st;
+    return from_cuda(launch_fused_grouped(p, input_grouped, static_cast<const __half *>(offset),
+                                          static_cast<const __half *>(mask),
+                                          static_cast<const uint8_t *>(packed_weight),
+                                          static_cast<const __half *>(bias), static_cast<__half *>(output),
+                                          nonfinite_flag, dev->sm_count, dev->err_word,
+                                          reinterpret_cast<cudaStream_t>(stream)));
 }
 
 dcn_status dcn_flag_non_finite_f16(const void *values, int64_t count, uint32_t *flag, dcn_stream stream) {

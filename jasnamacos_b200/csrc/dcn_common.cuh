@@ -98,16 +98,20 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
 // false) after kWaitLimitNs, or as soon as *abort becomes non-zero when `abort`
 // is given, so a broken pipeline ends the kernel with an error status instead
 // of hanging the GPU.
+// `backoff_ns` > 0 sleeps between polls (for waiters off the critical path, so
+// their polling does not take issue slots and shared-memory cycles).
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t parity,
-                                                  volatile int *abort) {
+                                                  volatile int *abort, uint32_t backoff_ns = 0) {
     if (mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = global_timer_ns();
     while (true) {
+        if (backoff_ns) __nanosleep(backoff_ns);
         if (mbar_try_wait(bar, parity)) return true;
         if (abort != nullptr && *abort) return false;
         if (global_timer_ns() - t0 > kWaitLimitNs) return false;
     }
 }
+
 
 // ---- TMA / bulk copies (no cluster multicast anywhere) --------------------------
 
@@ -131,6 +135,15 @@ __device__ __forceinline__ void tma_load_3d(void *smem_dst, const void *tensor_m
 
 __device__ __forceinline__ void prefetch_tensor_map(const void *tensor_map) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(tensor_map) : "memory");
+}
+
+// 32-byte read-only global load (sm_100: 256-bit vector load); `p` must be
+// 32-byte aligned.  volatile: the load must never be hoisted out of the bounds
+// check that guards it.
+__device__ __forceinline__ void ldg_nc_256(const void *p, uint32_t *r) {
+    asm volatile("ld.global.nc.v8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+        : "l"(p));
 }
 
 // ---- tcgen05 / tensor memory ------------------------------------------------------

@@ -47,7 +47,8 @@ constexpr int kChunksPerStage = 8;      // 8 x 8 channels = 64 K-elements
 constexpr int kStages = 4;              // A (TMEM) and offset/mask (smem) ring depth
 constexpr int kMaxKBlocks = 18;         // resident weight K-blocks (18 x 64 = 1152)
 constexpr int kBBlockBytes = BN * 128;  // one 64-wide K-block of B: 64 rows x 128 B
-constexpr int kThreads = 14 * 32;
+constexpr int kThreads = 16 * 32;  // 4 warpgroups: control (loader, MMA), epilogue, 2 x producers
+constexpr uint32_t kIdleBackoffNs = 200;
 constexpr int kProducerWarps = 8;
 constexpr int kEpilogueWarps = 4;
 constexpr int kOffRows = 2 * kChunksPerStage;  // offset channels per stage
@@ -63,6 +64,7 @@ struct __align__(1024) Smem {
     __half off[kStages][kOffRows][BM];     // offset rows of the stage (TMA box)
     __half msk[kStages][kMaskRows][BM];    // mask rows of the stage (TMA box)
     float bias[BN];
+    int4 chunk[kMaxKBlocks * kChunksPerStage];  // per K-chunk: {group entry offset, ky*DH, kx*DW, real}
     uint64_t om_full[kStages];   // TMA landed offsets/masks
     uint64_t om_empty[kStages];  // producers finished reading them
     uint64_t a_full[kStages];    // producers wrote the A stage into TMEM
@@ -76,7 +78,7 @@ struct __align__(1024) Smem {
 
 struct Args {
     Params p;
-    const uint4 *in8;          // input regrouped to [N][C/8][H][W][8] FP16 (16 B per position)
+    const uint4 *pairs;        // input regrouped to corner pairs, see regroup_pairs_kernel
     const uint8_t *packed_w;   // kb * kBBlockBytes bytes, prepacked
     const __half *bias;        // [64]
     __half *out;               // [N][64][HO][WO]
@@ -98,6 +100,15 @@ __device__ __forceinline__ void signal_abort(Smem &s, uint32_t *err) {
 __device__ __forceinline__ uint32_t pack_half2(__half2 h) {
     return *reinterpret_cast<uint32_t *>(&h);
 }
+
+// Per-thread state of one stage: the two 32-byte row loads of each of the
+// thread's 4 chunks, and the fractional sample position + mask needed to weight
+// them once they land.
+struct StageRegs {
+    uint32_t v[4][16];   // [chunk][row y0: 0..7 | row y0+1: 8..15], FP16 x 16 per row pair
+    uint32_t frac[4];    // half2 (ly, lx)
+    uint32_t msk[4];     // half mask in the low 16 bits, 0 for padding chunks
+};
 
 __global__ void __launch_bounds__(kThreads, 1)
     fused_dcn_kernel(const __grid_constant__ CUtensorMap tmap_off,
@@ -126,6 +137,16 @@ __global__ void __launch_bounds__(kThreads, 1)
         fence_mbarrier_init();
     }
     if (threadIdx.x < BN) s.bias[threadIdx.x] = __half2float(a.bias[threadIdx.x]);
+    for (int j = threadIdx.x; j < a.kb * kChunksPerStage; j += blockDim.x) {
+        int4 info = make_int4(0, 0, 0, 0);
+        if (j < a.nchunks) {
+            const int g = j / p.KA;
+            const int k = j - g * p.KA;
+            const int ky = k / p.KW;
+            info = make_int4(g * p.H * (p.W + 1), ky * p.DH, (k - ky * p.KW) * p.DW, 1);
+        }
+        s.chunk[j] = info;
+    }
     if (warp == 1) {
         tmem_alloc(&s.tmem_base, kTmemCols);
         tmem_relinquish();
@@ -138,10 +159,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = s.tmem_base;
+    const int wg = warp / 4;  // warpgroup: 0 control, 1 epilogue, 2-3 producers
 
-    if (warp == 0) {
-        // ------------------------------------------------------------ loader
-        if (lane == 0) {
+    if (wg == 0) {
+        if (warp == 0 && lane == 0) {
+            // ------------------------------------------------------------ loader
             mbar_arrive_expect_tx(&s.w_full, static_cast<uint32_t>(a.kb) * kBBlockBytes);
             for (int b = 0; b < a.kb; ++b)
                 bulk_copy_g2s(s.b[b], a.packed_w + static_cast<size_t>(b) * kBBlockBytes, kBBlockBytes, &s.w_full);
@@ -169,10 +191,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const uint32_t last = it - 1 - k;
                 mbar_wait_bounded(&s.om_full[last % kStages], (last / kStages) & 1u, nullptr);
             }
-        }
-    } else if (warp == 1) {
-        // --------------------------------------------------------------- MMA
-        if (lane == 0) {
+        } else if (warp == 1 && lane == 0) {
+            // --------------------------------------------------------------- MMA
             const uint32_t idesc = make_idesc_f16_f32(BM, BN);
             const uint32_t b_base = smem_addr(&s.b[0][0]);
             bool ok = mbar_wait_bounded(&s.w_full, 0, abort_flag);
@@ -220,7 +240,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             // Drain: the last commit arrives only after every MMA issued before it completed.
             if (last_bar != nullptr) mbar_wait_bounded(last_bar, last_parity, nullptr);
         }
-    } else if (warp < 2 + kEpilogueWarps) {
+    } else if (wg == 1) {
         // ---------------------------------------------------------- epilogue
         const int q = warp % 4;  // TMEM lane quarter this warp may access
         const int r = q * 32 + lane;
@@ -229,7 +249,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int tile = blockIdx.x; tile < a.num_tiles; tile += gridDim.x, ++tcount) {
             const uint32_t buf = tcount & 1u;
             const uint32_t bph = (tcount >> 1) & 1u;
-            if (!mbar_wait_bounded(&s.acc_full[buf], bph, abort_flag)) {
+            if (!mbar_wait_bounded(&s.acc_full[buf], bph, abort_flag, kIdleBackoffNs)) {
                 signal_abort(s, a.err);
                 break;
             }
@@ -259,108 +279,127 @@ __global__ void __launch_bounds__(kThreads, 1)
             atomicOr(a.flag, DCN_FLAG_NONFINITE);
     } else {
         // --------------------------------------------------------- producers
-        const int pw = warp - (2 + kEpilogueWarps);  // 0..7
-        const int q = warp % 4;                      // TMEM lane quarter
-        const int half_sel = pw / 4;                 // which 4 chunks of each stage
-        const int r = q * 32 + lane;                 // tile row = pixel
+        const int q = warp % 4;                  // TMEM lane quarter
+        const int half_sel = wg - 2;             // which 4 chunks of each stage
+        const int r = q * 32 + lane;             // tile row = pixel
         const uint32_t lane_base = tmem + (static_cast<uint32_t>(q * 32) << 16);
-        const int HW = p.in_plane;
-        uint32_t it = 0;
-        bool ok = true;
-        for (int tile = blockIdx.x; tile < a.num_tiles && ok; tile += gridDim.x) {
+        const int row_entries = p.W + 1;
+        const int local_tiles = (a.num_tiles - static_cast<int>(blockIdx.x) + static_cast<int>(gridDim.x) - 1) /
+                                static_cast<int>(gridDim.x);
+        const uint32_t total = static_cast<uint32_t>(local_tiles) * static_cast<uint32_t>(a.kb);
+
+        // Where the prefetch pointer is: stage `pf_sb` of local tile `pf_tile`, and that
+        // tile's per-pixel constants (recomputed once per tile, not per stage).
+        int pf_tile = -1, pf_sb = 0;
+        bool pf_valid = false;
+        int pf_base_y = 0, pf_base_x = 0;
+        const uint4 *pf_img = a.pairs;
+        auto enter_tile = [&](int local_tile) {
+            const int tile = static_cast<int>(blockIdx.x) + local_tile * static_cast<int>(gridDim.x);
             const int n = tile / a.tiles_per_image;
             const int px = (tile % a.tiles_per_image) * BM + r;
-            const bool valid = px < p.out_plane;
-            const int oy = valid ? px / p.WO : 0;
-            const int ox = valid ? px % p.WO : 0;
-            const int base_y = oy * p.SH - p.PH;
-            const int base_x = ox * p.SW - p.PW;
-            const uint4 *img = a.in8 + static_cast<size_t>(n) * p.OG * HW;
-            for (int sb = 0; sb < a.kb; ++sb, ++it) {
-                const uint32_t st = it % kStages;
-                const uint32_t ph = (it / kStages) & 1u;
-                if (!mbar_wait_bounded(&s.a_empty[st], ph ^ 1u, abort_flag) ||
-                    !mbar_wait_bounded(&s.om_full[st], ph, abort_flag)) {
-                    signal_abort(s, a.err);
-                    ok = false;
-                    break;
-                }
-                tc_fence_after();
+            pf_tile = local_tile;
+            pf_valid = px < p.out_plane;
+            const int oy = pf_valid ? px / p.WO : 0;
+            const int ox = pf_valid ? px - oy * p.WO : 0;
+            pf_base_y = oy * p.SH - p.PH;
+            pf_base_x = ox * p.SW - p.PW;
+            pf_img = a.pairs + static_cast<size_t>(n) * p.OG * p.H * row_entries * 2;
+        };
 
-                // Issue all 16 corner loads of the 4 chunks before using any.
-                uint4 v[4][4];
-                __half2 w[4][4];
-#pragma unroll
-                for (int c4 = 0; c4 < 4; ++c4) {
-                    const int c = half_sel * 4 + c4;
-                    const int j = sb * kChunksPerStage + c;
-#pragma unroll
-                    for (int t = 0; t < 4; ++t) v[c4][t] = make_uint4(0u, 0u, 0u, 0u);
-                    float w00 = 0.f, w01 = 0.f, w10 = 0.f, w11 = 0.f;
-                    if (valid && j < a.nchunks) {
-                        const int g = j / p.KA;
-                        const int k = j - g * p.KA;
-                        const int ky = k / p.KW;
-                        const int kx = k - ky * p.KW;
-                        const float off_y = __half2float(s.off[st][2 * c][r]);
-                        const float off_x = __half2float(s.off[st][2 * c + 1][r]);
-                        const float m = __half2float(s.msk[st][c][r]);
-                        const float y = static_cast<float>(base_y + ky * p.DH) + off_y;
-                        const float x = static_cast<float>(base_x + kx * p.DW) + off_x;
-                        const int y0 = __float2int_rd(y);
-                        const int x0 = __float2int_rd(x);
-                        const float ly = y - static_cast<float>(y0);
-                        const float lx = x - static_cast<float>(x0);
-                        const float hy = 1.0f - ly;
-                        const float hx = 1.0f - lx;
-                        const bool y0in = static_cast<unsigned>(y0) < static_cast<unsigned>(p.H);
-                        const bool y1in = static_cast<unsigned>(y0 + 1) < static_cast<unsigned>(p.H);
-                        const bool x0in = static_cast<unsigned>(x0) < static_cast<unsigned>(p.W);
-                        const bool x1in = static_cast<unsigned>(x0 + 1) < static_cast<unsigned>(p.W);
-                        const uint4 *gplane = img + static_cast<size_t>(g) * HW;
-                        const int idx = y0 * p.W + x0;
-                        if (y0in && x0in) v[c4][0] = __ldg(gplane + idx);
-                        if (y0in && x1in) v[c4][1] = __ldg(gplane + idx + 1);
-                        if (y1in && x0in) v[c4][2] = __ldg(gplane + idx + p.W);
-                        if (y1in && x1in) v[c4][3] = __ldg(gplane + idx + p.W + 1);
-                        w00 = hy * hx * m;
-                        w01 = hy * lx * m;
-                        w10 = ly * hx * m;
-                        w11 = ly * lx * m;
-                    }
-                    w[c4][0] = __float2half2_rn(w00);
-                    w[c4][1] = __float2half2_rn(w01);
-                    w[c4][2] = __float2half2_rn(w10);
-                    w[c4][3] = __float2half2_rn(w11);
-                }
-                // The offset/mask rows of this stage are no longer needed.
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&s.om_empty[st]);
-
-#pragma unroll
-                for (int c4 = 0; c4 < 4; ++c4) {
-                    const __half2 *h00 = reinterpret_cast<const __half2 *>(&v[c4][0]);
-                    const __half2 *h01 = reinterpret_cast<const __half2 *>(&v[c4][1]);
-                    const __half2 *h10 = reinterpret_cast<const __half2 *>(&v[c4][2]);
-                    const __half2 *h11 = reinterpret_cast<const __half2 *>(&v[c4][3]);
-                    uint32_t out[4];
-#pragma unroll
-                    for (int e = 0; e < 4; ++e) {
-                        __half2 acc = __hmul2(w[c4][0], h00[e]);
-                        acc = __hfma2(w[c4][1], h01[e], acc);
-                        acc = __hfma2(w[c4][2], h10[e], acc);
-                        acc = __hfma2(w[c4][3], h11[e], acc);
-                        out[e] = pack_half2(acc);
-                    }
-                    const int c = half_sel * 4 + c4;
-                    tmem_st_32x32b_x4(lane_base + kACol0 + st * kAStageCols + c * 4, out[0], out[1], out[2], out[3]);
-                }
-                tmem_wait_st();
-                tc_fence_before();
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&s.a_full[st]);
+        // Stage `itp` (the next one in order): read this pixel's offsets/masks of its 4
+        // chunks and issue the 8 row loads.
+        auto prefetch = [&](uint32_t itp, StageRegs &R) -> bool {
+            const uint32_t st = itp % kStages;
+            const uint32_t ph = (itp / kStages) & 1u;
+            if (pf_tile < 0 || pf_sb == a.kb) {
+                enter_tile(pf_tile + 1);
+                pf_sb = 0;
             }
-        }
+            const int sb = pf_sb++;
+            const bool valid = pf_valid;
+            const int base_y = pf_base_y, base_x = pf_base_x;
+            const uint4 *img = pf_img;
+            if (!mbar_wait_bounded(&s.om_full[st], ph, abort_flag)) return false;
+#pragma unroll
+            for (int c4 = 0; c4 < 4; ++c4) {
+                const int c = half_sel * 4 + c4;
+                const int4 info = s.chunk[sb * kChunksPerStage + c];
+#pragma unroll
+                for (int t = 0; t < 16; ++t) R.v[c4][t] = 0u;
+                R.frac[c4] = 0u;
+                R.msk[c4] = 0u;
+                if (valid && info.w) {
+                    const float off_y = __half2float(s.off[st][2 * c][r]);
+                    const float off_x = __half2float(s.off[st][2 * c + 1][r]);
+                    const float y = static_cast<float>(base_y + info.y) + off_y;
+                    const float x = static_cast<float>(base_x + info.z) + off_x;
+                    const int y0 = __float2int_rd(y);
+                    const int x0 = __float2int_rd(x);
+                    // Entry x0+1 of a row holds the corner pair (x0, x0+1), zero-padded
+                    // outside the image, so only rows need a bounds check here.
+                    const bool xin = static_cast<unsigned>(x0 + 1) <= static_cast<unsigned>(p.W);
+                    const bool y0in = xin && static_cast<unsigned>(y0) < static_cast<unsigned>(p.H);
+                    const bool y1in = xin && static_cast<unsigned>(y0 + 1) < static_cast<unsigned>(p.H);
+                    const uint4 *e0 = img + 2 * (static_cast<size_t>(info.x) + y0 * row_entries + (x0 + 1));
+                    if (y0in) ldg_nc_256(e0, &R.v[c4][0]);
+                    if (y1in) ldg_nc_256(e0 + 2 * row_entries, &R.v[c4][8]);
+                    R.frac[c4] = pack_half2(__floats2half2_rn(y - static_cast<float>(y0), x - static_cast<float>(x0)));
+                    R.msk[c4] = static_cast<uint32_t>(__half_as_ushort(s.msk[st][c][r]));
+                }
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&s.om_empty[st]);
+            return true;
+        };
+
+        // Stage `itc`: bilinear-combine the landed rows and store the A stage into TMEM.
+        auto commit = [&](uint32_t itc, StageRegs &R) -> bool {
+            const uint32_t st = itc % kStages;
+            const uint32_t ph = (itc / kStages) & 1u;
+            uint32_t outw[4][4];
+#pragma unroll
+            for (int c4 = 0; c4 < 4; ++c4) {
+                const float2 f = __half22float2(*reinterpret_cast<const __half2 *>(&R.frac[c4]));
+                const float m = __half2float(__ushort_as_half(static_cast<unsigned short>(R.msk[c4])));
+                const float mhy = m * (1.0f - f.x);
+                const float mly = m * f.x;
+                const __half2 w00 = __float2half2_rn(mhy * (1.0f - f.y));
+                const __half2 w01 = __float2half2_rn(mhy * f.y);
+                const __half2 w10 = __float2half2_rn(mly * (1.0f - f.y));
+                const __half2 w11 = __float2half2_rn(mly * f.y);
+                const __half2 *h = reinterpret_cast<const __half2 *>(&R.v[c4][0]);
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    __half2 acc = __hmul2(w00, h[e]);
+                    acc = __hfma2(w01, h[4 + e], acc);
+                    acc = __hfma2(w10, h[8 + e], acc);
+                    acc = __hfma2(w11, h[12 + e], acc);
+                    outw[c4][e] = pack_half2(acc);
+                }
+            }
+            if (!mbar_wait_bounded(&s.a_empty[st], ph ^ 1u, abort_flag)) return false;
+            tc_fence_after();
+#pragma unroll
+            for (int c4 = 0; c4 < 4; ++c4) {
+                const int c = half_sel * 4 + c4;
+                tmem_st_32x32b_x4(lane_base + kACol0 + st * kAStageCols + c * 4, outw[c4][0], outw[c4][1],
+                                  outw[c4][2], outw[c4][3]);
+            }
+            tmem_wait_st();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&s.a_full[st]);
+            return true;
+        };
+
+        // One stage at a time: issue its 8 row loads, then combine and store.  (Keeping
+        // two stages in flight per thread, with the producers given more registers by
+        // setmaxnreg, was measured slower and produced rare wrong A stages.)
+        StageRegs R;
+        bool ok = true;
+        for (uint32_t it = 0; ok && it < total; ++it) ok = prefetch(it, R) && commit(it, R);
+        if (!ok) signal_abort(s, a.err);
     }
 
     tc_fence_before();
@@ -369,27 +408,36 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (warp == 1) tmem_dealloc(tmem, kTmemCols);
 }
 
-// NCHW FP16 -> [N][C/8][H][W][8] FP16, so that one 16-byte load fetches the 8
-// channels of an offset group at one position.
-__global__ void __launch_bounds__(256) regroup_nchw_to_c8_kernel(const __half *__restrict__ in,
-                                                                  uint4 *__restrict__ out, int C,
-                                                                  int plane, int64_t total) {
-    const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;  // (n, cb, pixel)
+// NCHW FP16 -> corner pairs.  Entry (n, g, y, e), e = 0..W, is 32 bytes: the 8
+// channels of offset group g at (y, e-1) followed by the same channels at (y, e),
+// each half zero where the column is outside the image.  A bilinear sample whose
+// left corner is column x0 (-1 <= x0 <= W-1) then reads its two corners of one
+// row with a single aligned 32-byte load of entry x0+1.
+__global__ void __launch_bounds__(256) regroup_pairs_kernel(const __half *__restrict__ in,
+                                                             uint4 *__restrict__ out, int C, int H, int W,
+                                                             int64_t total) {
+    const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;  // entry index
     if (i >= total) return;
-    const int pix = static_cast<int>(i % plane);
-    const int64_t ncb = i / plane;
-    const int cb = static_cast<int>(ncb % (C / 8));
-    const int64_t n = ncb / (C / 8);
-    const __half *src = in + (n * C + cb * 8) * static_cast<int64_t>(plane) + pix;
-    __half h[8];
+    const int e = static_cast<int>(i % (W + 1));
+    const int64_t rest = i / (W + 1);
+    const int y = static_cast<int>(rest % H);
+    const int64_t ng = rest / H;  // n * (C/8) + g
+    const int64_t plane = static_cast<int64_t>(H) * W;
+    const __half *src = in + ng * 8 * plane + static_cast<int64_t>(y) * W;
+    const __half zero = __float2half_rn(0.0f);
+    uint32_t w[8];
 #pragma unroll
-    for (int e = 0; e < 8; ++e) h[e] = src[static_cast<int64_t>(e) * plane];
-    uint4 o;
-    o.x = pack_half2(__halves2half2(h[0], h[1]));
-    o.y = pack_half2(__halves2half2(h[2], h[3]));
-    o.z = pack_half2(__halves2half2(h[4], h[5]));
-    o.w = pack_half2(__halves2half2(h[6], h[7]));
-    out[i] = o;
+    for (int half_sel = 0; half_sel < 2; ++half_sel) {
+        const int x = e - 1 + half_sel;
+        const bool in_row = x >= 0 && x < W;
+        __half h[8];
+#pragma unroll
+        for (int c = 0; c < 8; ++c) h[c] = in_row ? src[c * plane + x] : zero;
+#pragma unroll
+        for (int c = 0; c < 4; ++c) w[half_sel * 4 + c] = pack_half2(__halves2half2(h[2 * c], h[2 * c + 1]));
+    }
+    out[2 * i] = make_uint4(w[0], w[1], w[2], w[3]);
+    out[2 * i + 1] = make_uint4(w[4], w[5], w[6], w[7]);
 }
 
 // ---------------------------------------------------------------- host side
@@ -435,7 +483,7 @@ bool fused_supported(const Params &p) {
     const int kb = (nchunks + fused::kChunksPerStage - 1) / fused::kChunksPerStage;
     if (kb > fused::kMaxKBlocks) return false;
     if (p.out_plane % 8 != 0) return false;
-    if (static_cast<int64_t>(p.N) * p.OG * p.in_plane >= (int64_t{1} << 31)) return false;
+    if (static_cast<int64_t>(p.OG) * p.H * (p.W + 1) >= (int64_t{1} << 31)) return false;
     return true;
 }
 
@@ -444,7 +492,8 @@ int fused_kblocks(const Params &p) {
 }
 
 size_t fused_workspace_bytes(const Params &p) {
-    const size_t bytes = static_cast<size_t>(p.N) * p.C * p.in_plane * sizeof(__half);
+    // corner pairs: N * (C/8) * H * (W+1) entries of 32 bytes
+    const size_t bytes = static_cast<size_t>(p.N) * (p.C / 8) * p.H * (p.W + 1) * 32;
     return (bytes + 255) & ~static_cast<size_t>(255);
 }
 
@@ -454,6 +503,10 @@ cudaError_t fused_prepare_device(uint32_t **err_word) {
     cudaError_t e = cudaFuncSetAttribute(fused::fused_dcn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          static_cast<int>(sizeof(fused::Smem) + 1024));
     if (e != cudaSuccess) return e;
+    cudaFuncAttributes attr;
+    e = cudaFuncGetAttributes(&attr, fused::fused_dcn_kernel);
+    if (e != cudaSuccess) return e;
+    if (attr.maxThreadsPerBlock < fused::kThreads) return cudaErrorInvalidConfiguration;
     void *ptr = nullptr;
     e = cudaGetSymbolAddress(&ptr, fused::g_error_word);
     if (e != cudaSuccess) return e;
@@ -461,26 +514,27 @@ cudaError_t fused_prepare_device(uint32_t **err_word) {
     return cudaSuccess;
 }
 
-cudaError_t launch_fused_f16(const Params &p, const __half *input, const __half *offset, const __half *mask,
-                             const uint8_t *packed_w, const __half *bias, __half *output, uint32_t *flag,
-                             void *workspace, int sm_count, uint32_t *err, cudaStream_t stream) {
-    using namespace fused;
-    // 1) regroup the input so each offset group's 8 channels are 16 contiguous bytes.
-    uint4 *in8 = static_cast<uint4 *>(workspace);
-    const int64_t total = static_cast<int64_t>(p.N) * (p.C / 8) * p.in_plane;
-    regroup_nchw_to_c8_kernel<<<static_cast<unsigned>((total + 255) / 256), 256, 0, stream>>>(
-        input, in8, p.C, p.in_plane, total);
-    cudaError_t e = cudaGetLastError();
-    if (e != cudaSuccess) return e;
+// NCHW FP16 -> corner pairs (the layout the fused kernel gathers from).
+cudaError_t launch_regroup_c8(const Params &p, const __half *input, void *workspace, cudaStream_t stream) {
+    const int64_t total = static_cast<int64_t>(p.N) * (p.C / 8) * p.H * (p.W + 1);
+    fused::regroup_pairs_kernel<<<static_cast<unsigned>((total + 255) / 256), 256, 0, stream>>>(
+        input, static_cast<uint4 *>(workspace), p.C, p.H, p.W, total);
+    return cudaGetLastError();
+}
 
-    // 2) fused gather + tcgen05 kernel, one persistent CTA per SM.
+// The fused gather + tcgen05 kernel on a regrouped input, one persistent CTA per SM.
+cudaError_t launch_fused_grouped(const Params &p, const void *input_c8, const __half *offset,
+                                 const __half *mask, const uint8_t *packed_w, const __half *bias,
+                                 __half *output, uint32_t *flag, int sm_count, uint32_t *err,
+                                 cudaStream_t stream) {
+    using namespace fused;
     CUtensorMap tmap_off, tmap_msk;
     if (!make_plane_map(&tmap_off, offset, p.out_plane, 2 * p.OG * p.KA, p.N, kOffRows) ||
         !make_plane_map(&tmap_msk, mask, p.out_plane, p.OG * p.KA, p.N, kMaskRows))
         return cudaErrorInvalidValue;
     Args a;
     a.p = p;
-    a.in8 = in8;
+    a.pairs = static_cast<const uint4 *>(input_c8);
     a.packed_w = packed_w;
     a.bias = bias;
     a.out = output;

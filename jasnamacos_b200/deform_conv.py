@@ -341,6 +341,33 @@ class CudaDeformConv:
         raise_for_status(st, "dcn_forward_f16")
         return out
 
+    def regroup_input(self, shape, input, workspace=None, stream=None):
+        """NCHW FP16 -> the fused kernel's [N][C/8][H][W][8] layout (the pre-pass of forward_f16)."""
+        torch = _torch()
+        ws_bytes = self.workspace_bytes(shape)
+        if ws_bytes == 0:
+            raise Unsupported("shape does not take the fused path")
+        if workspace is None:
+            workspace = torch.empty(ws_bytes, dtype=torch.uint8, device=input.device)
+        self._check_device(input, workspace)
+        st = self.lib.dcn_regroup_input_f16(ctypes.byref(shape.to_c()), _ptr(input), _ptr(workspace),
+                                            workspace.numel() * workspace.element_size(), _stream_handle(stream))
+        raise_for_status(st, "dcn_regroup_input_f16")
+        return workspace
+
+    def forward_f16_grouped(self, shape, input_grouped, offset, mask, packed_weight, bias, out=None, flag=None,
+                            stream=None):
+        """The fused gather + tcgen05 kernel alone, on an input already in the grouped layout."""
+        torch = _torch()
+        if out is None:
+            out = torch.empty(shape.output_count, dtype=torch.float16, device=offset.device)
+        self._check_device(input_grouped, offset, mask, packed_weight, bias, out, flag)
+        st = self.lib.dcn_forward_f16_grouped(
+            ctypes.byref(shape.to_c()), _ptr(input_grouped), _ptr(offset), _ptr(mask), _ptr(packed_weight),
+            _ptr(bias), _ptr(out), _ptr(flag), _stream_handle(stream))
+        raise_for_status(st, "dcn_forward_f16_grouped")
+        return out
+
     def flag_non_finite(self, values, flag, stream=None):
         """flag_non_finite_fp16 (MetalShader.swift:454-463)."""
         self._check_device(values, flag)
@@ -366,6 +393,63 @@ class CudaDeformConv:
     def device_error(self) -> None:
         """Raises DeviceTimeout if a kernel's bounded device-side wait expired since the last check."""
         raise_for_status(self.lib.dcn_device_error(), "device error word")
+
+    def forward_f16_host(self, shape, input_host, offset_host, mask_host, packed_weight, bias, out_host,
+                         chunk_images: int | None = None, slots: int = 2):
+        """End-to-end FP16 operator on HOST buffers: the batch is cut into chunks of images and
+        each chunk's input/offset/mask are copied host->device, convolved by the fused kernel and
+        copied back, with `slots` chunks in flight on separate streams so copies in both
+        directions overlap the kernel.  Host tensors should be pinned (torch pin_memory) for
+        asynchronous copies.  Returns the non-finite flag (int) after synchronising; raises
+        NonFiniteOutput if it is set."""
+        torch = _torch()
+        dev = packed_weight.device
+        n = shape.batch
+        if chunk_images is None:
+            chunk_images = max(1, min(n, 64))
+        chunk_images = max(1, min(chunk_images, n))
+        one = shape.with_batch(1)
+        per = (one.input_count, one.offset_count, one.mask_count, one.output_count)
+        cshape = shape.with_batch(chunk_images)
+        ws_bytes = self.workspace_bytes(cshape)
+        bufs = []
+        for _ in range(slots):
+            bufs.append({
+                "x": torch.empty(chunk_images * per[0], dtype=torch.float16, device=dev),
+                "off": torch.empty(chunk_images * per[1], dtype=torch.float16, device=dev),
+                "msk": torch.empty(chunk_images * per[2], dtype=torch.float16, device=dev),
+                "out": torch.empty(chunk_images * per[3], dtype=torch.float16, device=dev),
+                "ws": torch.empty(max(ws_bytes, 16), dtype=torch.uint8, device=dev),
+                "stream": torch.cuda.Stream(device=dev),
+                "done": None,
+            })
+        flag = torch.zeros(1, dtype=torch.int32, device=dev)
+        main = torch.cuda.current_stream(dev)
+        for ci, b0 in enumerate(range(0, n, chunk_images)):
+            b1 = min(n, b0 + chunk_images)
+            k = b1 - b0
+            slot = bufs[ci % slots]
+            st = slot["stream"]
+            st.wait_stream(main)
+            if slot["done"] is not None:
+                st.wait_event(slot["done"])
+            with torch.cuda.stream(st):
+                slot["x"][: k * per[0]].copy_(input_host[b0 * per[0]:b1 * per[0]], non_blocking=True)
+                slot["off"][: k * per[1]].copy_(offset_host[b0 * per[1]:b1 * per[1]], non_blocking=True)
+                slot["msk"][: k * per[2]].copy_(mask_host[b0 * per[2]:b1 * per[2]], non_blocking=True)
+                self.forward_f16(shape.with_batch(k), slot["x"][: k * per[0]], slot["off"][: k * per[1]],
+                                 slot["msk"][: k * per[2]], packed_weight, bias, out=slot["out"][: k * per[3]],
+                                 flag=flag, workspace=slot["ws"], stream=st)
+                out_host[b0 * per[3]:b1 * per[3]].copy_(slot["out"][: k * per[3]], non_blocking=True)
+                ev = torch.cuda.Event()
+                ev.record(st)
+                slot["done"] = ev
+        for slot in bufs:
+            main.wait_stream(slot["stream"])
+        value = int(flag.item())  # device -> host read of the step's result flag (synchronises)
+        if value & _native.DCN_FLAG_NONFINITE:
+            raise NonFiniteOutput("Inf/NaN in the DCNv2 output")
+        return value
 
     # -- host-array API (synchronous, like the reference) -------------------------
     def run_float32(self, shape: DeformConvShape, input, offset, mask, weight, bias) -> np.ndarray:

@@ -1,0 +1,45 @@
+"""Tile sharding across GPUs (one process per GPU).
+
+The DCNv2 path partitions naturally: each output tile depends only on its own input,
+offset and mask plus the replicated weights, so rank r of `world` processes a contiguous
+range of tiles and there is no collective on the data path.  The one exchange the
+production flow needs -- bringing every shard's output to one rank -- is
+:func:`gather_to_root`, used after (never inside) a timed step.
+"""
+
+from __future__ import annotations
+
+
+def shard_range(total: int, rank: int, world: int) -> tuple[int, int]:
+    """Tiles [begin, end) of `rank`: contiguous, sizes differ by at most one, every tile once."""
+    if world <= 0 or not 0 <= rank < world or total < 0:
+        raise ValueError(f"bad shard request total={total} rank={rank} world={world}")
+    return total * rank // world, total * (rank + 1) // world
+
+
+def gather_to_root(local, total_tiles: int, per_tile: int, dist, root: int = 0):
+    """Collects every rank's shard of a [tiles * per_tile] output onto `root`.
+
+    `local` is this rank's contiguous shard (a torch tensor); `dist` is
+    torch.distributed with an initialised process group (NCCL for CUDA tensors, gloo for
+    CPU).  Ranks exchange point-to-point (shards may differ in size by one tile).
+    Returns the full tensor on root and None elsewhere.  Every rank takes the same steps.
+    """
+    import torch
+
+    rank, world = dist.get_rank(), dist.get_world_size()
+    b, e = shard_range(total_tiles, rank, world)
+    if local.numel() != (e - b) * per_tile:
+        raise ValueError("local shard has the wrong size")
+    if rank != root:
+        dist.send(local.contiguous(), dst=root)
+        return None
+    full = torch.empty(total_tiles * per_tile, dtype=local.dtype, device=local.device)
+    full[b * per_tile:e * per_tile].copy_(local)
+    for src in range(world):
+        if src == root:
+            continue
+        sb, se = shard_range(total_tiles, src, world)
+        view = full[sb * per_tile:se * per_tile]
+        dist.recv(view, src=src)
+    return full

@@ -60,6 +60,9 @@ def load():
             lib.dcn_oracle_run_threads.argtypes = [sp, fp, fp, fp, fp, fp, fp, ctypes.c_int32, ctypes.c_int32,
                                                    ctypes.c_int, ctypes.c_int]
             lib.dcn_oracle_run_threads.restype = ctypes.c_int
+            lib.dcn_oracle_run_sample.argtypes = [sp, fp, fp, fp, fp, fp, fp, ctypes.c_int32, ctypes.c_int32,
+                                                  ctypes.c_int]
+            lib.dcn_oracle_run_sample.restype = ctypes.c_int
             lib.dcn_oracle_prepare_offsets.argtypes = [ctypes.c_int64, fp, fp, fp, fp, fp]
             lib.dcn_oracle_prepare_offsets.restype = None
             lib.dcn_oracle_splitmix64.argtypes = [ctypes.POINTER(ctypes.c_uint64)]
@@ -98,6 +101,21 @@ def run(shape, input, offset, mask, weight, bias, threads: int = 1, batch_range=
     if rc != 0:
         raise ValueError(f"oracle rejected the shape (rc={rc})")
     return out if batch_range is None else out[b * per_image:e * per_image].copy()
+
+
+def run_sample(shape, input, offset, mask, weight, bias, rows: tuple[int, int], threads: int) -> np.ndarray:
+    """The literal reference loop over output rows [rows[0], rows[1]) of every image, one
+    batch slice per thread (the CPU-baseline timing sample).  Returns the full output array
+    (untouched outside the rows)."""
+    lib = load()
+    s = _shape(shape)
+    arrays = [np.ascontiguousarray(a, dtype=np.float32).reshape(-1) for a in (input, offset, mask, weight, bias)]
+    out = np.zeros(s.batch * s.output_channels * s.output_height * s.output_width, dtype=np.float32)
+    rc = lib.dcn_oracle_run_sample(ctypes.byref(s), *[_fptr(a) for a in arrays], _fptr(out), rows[0], rows[1],
+                                   max(1, int(threads)))
+    if rc != 0:
+        raise ValueError(f"oracle rejected the shape (rc={rc})")
+    return out
 
 
 def prepare_offsets(plane: int, raw, flow1, flow2):

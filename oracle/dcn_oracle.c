@@ -76,10 +76,11 @@ static float bilinear(const float *input, int64_t base, int64_t height, int64_t 
     return r;
 }
 
-/* DeformConvCPU.run loop body (DeformConv.swift:98-136) for batch items [n_begin, n_end). */
-int dcn_oracle_run_range(const dcn_oracle_shape *s, const float *input, const float *offset,
-                         const float *mask, const float *weight, const float *bias, float *output,
-                         int32_t n_begin, int32_t n_end) {
+/* DeformConvCPU.run loop body (DeformConv.swift:98-136) for batch items
+ * [n_begin, n_end) and output rows [oy_begin, oy_end). */
+static int run_literal(const dcn_oracle_shape *s, const float *input, const float *offset,
+                       const float *mask, const float *weight, const float *bias, float *output,
+                       int32_t n_begin, int32_t n_end, int32_t oy_begin, int32_t oy_end) {
     if (dcn_oracle_validate(s)) return 1;
     const int64_t channels_per_group = s->input_channels / s->groups;
     const int64_t outputs_per_group = s->output_channels / s->groups;
@@ -93,7 +94,7 @@ int dcn_oracle_run_range(const dcn_oracle_shape *s, const float *input, const fl
     for (int64_t n = n_begin; n < n_end; ++n) {
         for (int64_t oc = 0; oc < s->output_channels; ++oc) {
             const int64_t group = oc / outputs_per_group;
-            for (int64_t oy = 0; oy < s->output_height; ++oy) {
+            for (int64_t oy = oy_begin; oy < oy_end; ++oy) {
                 for (int64_t ox = 0; ox < s->output_width; ++ox) {
                     float sum = bias[oc];
                     for (int64_t local_ic = 0; local_ic < channels_per_group; ++local_ic) {
@@ -147,6 +148,13 @@ int dcn_oracle_run_range(const dcn_oracle_shape *s, const float *input, const fl
         }
     }
     return 0;
+}
+
+int dcn_oracle_run_range(const dcn_oracle_shape *s, const float *input, const float *offset,
+                         const float *mask, const float *weight, const float *bias, float *output,
+                         int32_t n_begin, int32_t n_end) {
+    return run_literal(s, input, offset, mask, weight, bias, output, n_begin, n_end, 0,
+                       s->output_height);
 }
 
 int dcn_oracle_run(const dcn_oracle_shape *s, const float *input, const float *offset,
@@ -232,6 +240,56 @@ int dcn_oracle_run_fast_range(const dcn_oracle_shape *s, const float *input, con
     }
     free(sm);
     return 0;
+}
+
+typedef struct {
+    const dcn_oracle_shape *s;
+    const float *input, *offset, *mask, *weight, *bias;
+    float *output;
+    int32_t n_begin, n_end, oy_begin, oy_end;
+    int rc;
+} sample_job;
+
+static void *sample_worker(void *arg) {
+    sample_job *j = (sample_job *)arg;
+    j->rc = run_literal(j->s, j->input, j->offset, j->mask, j->weight, j->bias, j->output,
+                        j->n_begin, j->n_end, j->oy_begin, j->oy_end);
+    return NULL;
+}
+
+int dcn_oracle_run_sample(const dcn_oracle_shape *s, const float *input, const float *offset,
+                          const float *mask, const float *weight, const float *bias,
+                          float *output, int32_t oy_begin, int32_t oy_end, int threads) {
+    if (dcn_oracle_validate(s)) return 1;
+    if (oy_begin < 0) oy_begin = 0;
+    if (oy_end > s->output_height) oy_end = s->output_height;
+    if (threads <= 0) threads = 1;
+    if (threads > s->batch) threads = s->batch;
+    pthread_t *tid = (pthread_t *)malloc(sizeof(pthread_t) * (size_t)threads);
+    sample_job *jobs = (sample_job *)malloc(sizeof(sample_job) * (size_t)threads);
+    if (!tid || !jobs) {
+        free(tid);
+        free(jobs);
+        return 2;
+    }
+    int rc = 0;
+    for (int t = 0; t < threads; ++t) {
+        sample_job j = {s, input, offset, mask, weight, bias, output,
+                        (int32_t)((int64_t)s->batch * t / threads),
+                        (int32_t)((int64_t)s->batch * (t + 1) / threads), oy_begin, oy_end, 0};
+        jobs[t] = j;
+        if (pthread_create(&tid[t], NULL, sample_worker, &jobs[t]) != 0) {
+            sample_worker(&jobs[t]);
+            tid[t] = 0;
+        }
+    }
+    for (int t = 0; t < threads; ++t) {
+        if (tid[t]) pthread_join(tid[t], NULL);
+        if (jobs[t].rc) rc = jobs[t].rc;
+    }
+    free(tid);
+    free(jobs);
+    return rc;
 }
 
 typedef struct {

@@ -57,6 +57,14 @@ int dcn_oracle_run_threads(const dcn_oracle_shape *s, const float *input, const 
                            const float *mask, const float *weight, const float *bias,
                            float *output, int32_t n_begin, int32_t n_end, int threads, int fast);
 
+/* Bounded sample of the literal reference loop for CPU timing: output rows
+ * [oy_begin, oy_end) of every image, the batch split over `threads` POSIX
+ * threads (one contiguous slice each, single-threaded per image like the
+ * reference).  Outputs outside the rows are left untouched. */
+int dcn_oracle_run_sample(const dcn_oracle_shape *s, const float *input, const float *offset,
+                          const float *mask, const float *weight, const float *bias,
+                          float *output, int32_t oy_begin, int32_t oy_end, int threads);
+
 /* prepare_dcn_offsets_fp16 restated in FP32 (MetalShader.swift:817-839; the
  * reference's own CPU check is JasnaCLI.swift:177-211).  raw [432][plane],
  * flow1/flow2 [2][plane] in (x, y) order -> offset [288][plane], mask [144][plane]. */

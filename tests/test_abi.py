@@ -77,7 +77,8 @@ def test_path_selection_and_sizes(lib):
     jasna = DeformConvShape.jasna_propagation().to_c()
     assert lib.dcn_forward_f16_path(ctypes.byref(jasna)) == _native.DCN_PATH_FUSED_TC
     assert lib.dcn_packed_weight_bytes(ctypes.byref(jasna)) == 18 * 8192
-    assert lib.dcn_forward_f16_workspace_bytes(ctypes.byref(jasna)) == 128 * 64 * 64 * 2
+    # corner-pair regrouped input: (C/8) groups x H rows x (W+1) entries x 32 bytes
+    assert lib.dcn_forward_f16_workspace_bytes(ctypes.byref(jasna)) == 16 * 64 * 65 * 32
     # 32 output channels -> direct path, OIHW FP16 packed weight, no workspace.
     other = DeformConvShape(1, 128, 64, 64, 32, 64, 64, 3, 3, 1, 1, 1, 1, 1, 1, 1, 16).to_c()
     assert lib.dcn_forward_f16_path(ctypes.byref(other)) == _native.DCN_PATH_DIRECT

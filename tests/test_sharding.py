@@ -1,0 +1,96 @@
+"""Multi-rank host logic on CPU: tile partitioning and the output gather, with gloo ranks
+(world size 2 and 3), plus a rank that fails before the gather (the others must see an error,
+not hang)."""
+
+from __future__ import annotations
+
+import os
+import socket
+import sys
+from pathlib import Path
+
+import pytest
+
+from jasnamacos_b200.sharding import shard_range
+
+REPO = Path(__file__).resolve().parent.parent
+
+
+def test_shard_range_covers_every_tile_once():
+    for total in (0, 1, 7, 128, 2048):
+        for world in (1, 2, 3, 4, 8):
+            ranges = [shard_range(total, r, world) for r in range(world)]
+            assert ranges[0][0] == 0 and ranges[-1][1] == total
+            for (b0, e0), (b1, _) in zip(ranges, ranges[1:]):
+                assert e0 == b1
+            sizes = [e - b for b, e in ranges]
+            assert max(sizes) - min(sizes) <= 1
+    with pytest.raises(ValueError):
+        shard_range(10, 2, 2)
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _worker(rank, world, port, total, per_tile, fail_rank, q):
+    sys.path.insert(0, str(REPO))
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    from jasnamacos_b200.sharding import gather_to_root, shard_range
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=10))
+    try:
+        b, e = shard_range(total, rank, world)
+        local = torch.arange(b * per_tile, e * per_tile, dtype=torch.float32)  # "output" of my tiles
+        if rank == fail_rank:
+            raise RuntimeError("injected host-side failure before the gather")
+        full = gather_to_root(local, total, per_tile, dist)
+        if rank == 0:
+            q.put(("ok", bool(torch.equal(full, torch.arange(total * per_tile, dtype=torch.float32)))))
+        else:
+            q.put(("ok", full is None))
+    except Exception as exc:  # noqa: BLE001 - reported to the parent
+        q.put(("error", f"{rank}: {type(exc).__name__}"))
+    finally:
+        try:
+            dist.destroy_process_group()
+        except Exception:  # noqa: BLE001
+            pass
+
+
+def _run(world, total, per_tile, fail_rank=-1, timeout=60):
+    import multiprocessing as mp
+
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, world, port, total, per_tile, fail_rank, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    results = []
+    for _ in range(world):
+        results.append(q.get(timeout=timeout))
+    for p in procs:
+        p.join(timeout=timeout)
+        if p.is_alive():
+            p.kill()
+    return results
+
+
+@pytest.mark.parametrize("world,total", [(2, 7), (3, 16)])
+def test_gather_to_root_gloo(world, total):
+    results = _run(world, total, per_tile=5)
+    assert all(kind == "ok" and flag for kind, flag in results), results
+
+
+def test_failed_rank_surfaces_as_error_not_hang():
+    results = _run(2, 8, per_tile=3, fail_rank=1, timeout=90)
+    kinds = sorted(kind for kind, _ in results)
+    assert kinds == ["error", "error"], results  # rank 1 failed; rank 0's recv timed out or was aborted
