@@ -88,7 +88,8 @@ typedef enum dcn_status {
     DCN_ERR_NONFINITE = 5,        /* .nonFiniteOutput     DeformConv.swift:49,52-55 (the only recoverable one) */
     DCN_ERR_LAUNCH = 6,           /* .commandFailed       MetalRunner.swift:619-621 */
     DCN_ERR_INVALID_ARGUMENT = 7, /* NULL pointer / misaligned pointer / short workspace */
-    DCN_ERR_DEVICE_TIMEOUT = 8    /* a device-side bounded wait expired (pipeline error) */
+    DCN_ERR_DEVICE_TIMEOUT = 8,   /* a device-side bounded wait expired (pipeline error) */
+    DCN_ERR_SCRATCH_TOO_SMALL = 9 /* the problem needs more than the library's static scratch */
 } dcn_status;
 
 typedef enum dcn_dtype {
@@ -216,6 +217,25 @@ dcn_status dcn_flag_non_finite_f16(const void *values, int64_t count, uint32_t *
  * flipped flow, mask [144][plane] = sigmoid(raw).  All FP16. */
 dcn_status dcn_prepare_offsets_f16(int64_t plane, const void *raw, const void *flow1,
                                    const void *flow2, void *offset, void *mask, dcn_stream stream);
+
+/* ---- fused FP16 path without any caller allocation ----------------------------
+ * No counterpart in the reference.  For callers that cannot allocate device
+ * memory when they run the convolution (allocator-less or real-time regions,
+ * plugin hosts that own every device allocation): the same operator as
+ * dcn_forward_f16, but its scratch is a fixed array inside the library
+ * (dcn_static_scratch_bytes() = 16 MiB, held on every GPU that loads the
+ * library until the process exits), so the caller passes only inputs and outputs.
+ * Fused-path shapes only (else DCN_ERR_UNSUPPORTED); a problem whose scratch
+ * exceeds the array returns DCN_ERR_SCRATCH_TOO_SMALL (16 MiB holds 7 Jasna
+ * 64x64 tiles).  All calls share the array, so calls that overlap on the GPU race
+ * and must be ordered (one stream, or events).  The first call on a device looks
+ * up the array's address; make it before any stream capture.  Allocates nothing. */
+size_t dcn_static_scratch_bytes(void);
+dcn_status dcn_forward_f16_static_scratch(const dcn_shape *shape, const void *input,
+                                          const void *offset, const void *mask,
+                                          const void *packed_weight, const void *bias,
+                                          void *output, uint32_t *nonfinite_flag,
+                                          dcn_stream stream);
 
 /* ---- device error word ----------------------------------------------------------
  * Every kernel with a bounded device-side wait records a timeout in a sticky

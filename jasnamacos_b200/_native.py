@@ -23,6 +23,7 @@ DCN_ERR_NONFINITE = 5
 DCN_ERR_LAUNCH = 6
 DCN_ERR_INVALID_ARGUMENT = 7
 DCN_ERR_DEVICE_TIMEOUT = 8
+DCN_ERR_SCRATCH_TOO_SMALL = 9
 
 DCN_DTYPE_F32 = 0
 DCN_DTYPE_F16 = 1
@@ -97,6 +98,8 @@ PROTOTYPES = {
     "dcn_flag_non_finite_f16": (ctypes.c_int, [_P, ctypes.c_int64, _P, _P]),
     "dcn_prepare_offsets_f16": (ctypes.c_int, [ctypes.c_int64, _P, _P, _P, _P, _P, _P]),
     "dcn_device_error": (ctypes.c_int, []),
+    "dcn_static_scratch_bytes": (ctypes.c_size_t, []),
+    "dcn_forward_f16_static_scratch": (ctypes.c_int, [_SHAPE, _P, _P, _P, _P, _P, _P, _P, _P]),
 }
 
 

@@ -29,6 +29,7 @@ SOURCES = [
     "dcn_fused_sm100.cu",
     "dcn_prepack.cu",
     "dcn_aux.cu",
+    "dcn_static_scratch.cu",
 ]
 HEADERS = ["dcn_common.cuh"]
 

@@ -147,6 +147,8 @@ const char *dcn_status_string(dcn_status status) {
     case DCN_ERR_LAUNCH: return "CUDA launch failed";
     case DCN_ERR_INVALID_ARGUMENT: return "Invalid argument (null or misaligned pointer, short workspace)";
     case DCN_ERR_DEVICE_TIMEOUT: return "A device-side wait timed out (pipeline error)";
+    case DCN_ERR_SCRATCH_TOO_SMALL:
+        return "The problem needs more scratch than the library's static scratch array holds";
     }
     return "unknown status";
 }

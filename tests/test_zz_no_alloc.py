@@ -1,0 +1,70 @@
+"""GPU: dcn_forward_f16_static_scratch, the entry point for callers that cannot allocate
+device memory when they run the convolution (its scratch lives in a fixed 16 MiB array
+inside the library), called through the C ABI and compared with dcn_forward_f16 given a
+caller workspace, on two calls in a row with different inputs.  Collected last on purpose
+(file name), and self-contained, so it passes alone in a fresh process or after the rest."""
+
+from __future__ import annotations
+
+import ctypes
+
+import numpy as np
+import pytest
+
+from jasnamacos_b200 import _native, synthetic
+from jasnamacos_b200.deform_conv import DeformConvShape
+
+pytestmark = pytest.mark.gpu
+
+F16_MAX_ABS = 2e-2
+F16_MEAN_ABS = 2e-3
+
+
+def _p(t):
+    return ctypes.c_void_p(t.data_ptr())
+
+
+def test_static_scratch_matches_workspace_entry_point_twice():
+    import torch
+
+    assert torch.cuda.is_available()
+    lib = _native.load()
+    shape = DeformConvShape.jasna_propagation(batch=4)  # 4 x 2.03 MiB of scratch, under 16 MiB
+    c_shape = shape.to_c()
+    assert lib.dcn_static_scratch_bytes() == 16 << 20
+    w, b = synthetic.weights(shape, 21)
+    w16 = torch.from_numpy(w).cuda().half()
+    b16 = torch.from_numpy(b).cuda().half()
+    packed = torch.empty(lib.dcn_packed_weight_bytes(ctypes.byref(c_shape)), dtype=torch.uint8, device="cuda")
+    assert lib.dcn_prepack_weights(ctypes.byref(c_shape), _p(w16), _native.DCN_DTYPE_F16, _native.DCN_WEIGHT_OIHW,
+                                   _p(packed), None) == _native.DCN_OK
+    ws_bytes = lib.dcn_forward_f16_workspace_bytes(ctypes.byref(c_shape))
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device="cuda")
+
+    for call, seed in enumerate((31, 32)):  # two calls in a row, different inputs
+        x, off, msk, _, _ = synthetic.device_batch(shape, 16.0, seed=seed, device="cuda")
+        ref = torch.empty(shape.output_count, dtype=torch.float16, device="cuda")
+        out = torch.full((shape.output_count,), float("nan"), dtype=torch.float16, device="cuda")
+        flag = torch.zeros(1, dtype=torch.int32, device="cuda")
+        st = lib.dcn_forward_f16(ctypes.byref(c_shape), _p(x), _p(off), _p(msk), _p(packed), _p(b16), _p(ref),
+                                 None, _p(ws), ws_bytes, None)
+        assert st == _native.DCN_OK
+        st = lib.dcn_forward_f16_static_scratch(ctypes.byref(c_shape), _p(x), _p(off), _p(msk), _p(packed),
+                                                _p(b16), _p(out), _p(flag), None)
+        assert st == _native.DCN_OK, _native.status_string(st)
+        torch.cuda.synchronize()
+        assert int(flag.item()) == 0
+        d = (out.float() - ref.float()).abs().cpu().numpy()
+        assert np.isfinite(d).all(), f"call {call}: non-finite output"
+        assert float(d.max()) <= F16_MAX_ABS and float(d.mean()) <= F16_MEAN_ABS, (call, float(d.max()))
+
+
+def test_static_scratch_rejects_problems_beyond_its_size():
+    lib = _native.load()
+    big = DeformConvShape.jasna_propagation(batch=8)  # 8 x 2.03 MiB > 16 MiB
+    c_big = big.to_c()
+    assert lib.dcn_forward_f16_workspace_bytes(ctypes.byref(c_big)) > lib.dcn_static_scratch_bytes()
+    p = ctypes.c_void_p(16)  # never dereferenced: the size check comes first
+    st = lib.dcn_forward_f16_static_scratch(ctypes.byref(c_big), p, p, p, p, p, p, None, None)
+    assert st == _native.DCN_ERR_SCRATCH_TOO_SMALL
+    assert b"static scratch" in lib.dcn_status_string(st)
