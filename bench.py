@@ -307,8 +307,12 @@ def run_ours(args):
     torch.cuda.synchronize(dev)
     achieved_gbs = BYTES_PER_PX * px_per_step / (fused_ms * 1e-3) / 1e9
     tensor_tflops = FLOPS_PER_PX * px_per_step / (fused_ms * 1e-3) / 1e12
+    from jasnamacos_b200 import _native
+
+    kernel = {_native.DCN_PATH_SLAB_TC: "slab_dcn_kernel",
+              _native.DCN_PATH_FUSED_TC: "fused_dcn_kernel"}.get(op.path(shape), "direct_kernel")
     traffic = None
-    prof = REPO / "profiles" / "fused_dcn_traffic.json"
+    prof = REPO / "profiles" / f"{kernel}_traffic.json"
     if prof.exists():
         d = json.loads(prof.read_text())
         traffic = d.get("dram_bytes_per_output_px", 0) * px_per_step or None
@@ -382,7 +386,7 @@ def run_ours(args):
                        "parallelism": f"tile shards x{world}, no data-path collective"},
             "roofline": {"bound": "hbm", "achieved": achieved_gbs, "peak": peaks["hbm_gbs"], "unit": "GB/s",
                          "frac": achieved_gbs / peaks["hbm_gbs"], "traffic": traffic,
-                         "peak_source": f"{peak_kind} hbm_gbs", "kernel": "fused_dcn_kernel",
+                         "peak_source": f"{peak_kind} hbm_gbs", "kernel": kernel,
                          "kernel_ms": fused_ms, "regroup_ms": regroup_ms,
                          "algorithmic_bytes_per_px": BYTES_PER_PX,
                          "tensor_tflops": tensor_tflops,

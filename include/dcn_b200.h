@@ -110,7 +110,10 @@ typedef enum dcn_weight_layout {
 /* Implementation selected by dcn_forward_f16 for a given shape. */
 typedef enum dcn_path {
     DCN_PATH_DIRECT = 0,      /* CUDA-core direct kernel (any valid shape) */
-    DCN_PATH_FUSED_TC = 1     /* sm_100a fused gather + tcgen05 implicit GEMM */
+    DCN_PATH_FUSED_TC = 1,    /* sm_100a fused gather + tcgen05 implicit GEMM, gathers from
+                                 global memory (any image size) */
+    DCN_PATH_SLAB_TC = 2      /* the same operator with each deformable group's input staged
+                                 whole in shared memory (3x3 kernels, images up to ~70x70) */
 } dcn_path;
 
 /* ---- status / shape helpers ------------------------------------------------ */
@@ -171,7 +174,10 @@ size_t dcn_packed_weight_bytes(const dcn_shape *shape);
 dcn_status dcn_prepack_weights(const dcn_shape *shape, const void *weight, dcn_dtype src_dtype,
                                dcn_weight_layout src_layout, void *packed, dcn_stream stream);
 
-/* Which implementation dcn_forward_f16 runs for this shape. */
+/* Which implementation dcn_forward_f16 runs for this shape.  The choice between the
+ * two tensor-core kernels can be pinned for a process with the environment
+ * variable DCN_B200_FUSED_KERNEL=slab|pairs (default: slab where it applies),
+ * read once; packed weights and workspaces must come from the same process. */
 dcn_path dcn_forward_f16_path(const dcn_shape *shape);
 
 /* ---- fused FP16 path ----------------------------------------------------------
@@ -190,13 +196,13 @@ dcn_status dcn_forward_f16(const dcn_shape *shape, const void *input, const void
                            size_t workspace_bytes, dcn_stream stream);
 
 /* The two launches dcn_forward_f16 makes, for callers that keep their features
- * channels-last and for timing the fused kernel alone.
- * dcn_regroup_input_f16: NCHW FP16 input -> "group-blocked channels-last"
- *   [N][C/8][H][W][8] FP16 in `workspace` (dcn_forward_f16_workspace_bytes bytes),
- *   so the 8 channels of one deformable group at one position are 16 contiguous bytes.
- * dcn_forward_f16_grouped: the fused gather + tcgen05 kernel reading such a grouped
- *   input (16-byte aligned).  Both require dcn_forward_f16_path() == DCN_PATH_FUSED_TC
- *   and return DCN_ERR_UNSUPPORTED otherwise. */
+ * channels-last and for timing the tensor-core kernel alone.
+ * dcn_regroup_input_f16: NCHW FP16 input -> the grouped channels-last layout of the
+ *   selected path in `workspace` (dcn_forward_f16_workspace_bytes bytes): 8 channels
+ *   of one deformable group per 16 bytes, as zero-bordered per-group slabs
+ *   (DCN_PATH_SLAB_TC) or as 32-byte horizontal corner pairs (DCN_PATH_FUSED_TC).
+ * dcn_forward_f16_grouped: the tensor-core kernel reading such an input (16-byte
+ *   aligned).  Both return DCN_ERR_UNSUPPORTED for DCN_PATH_DIRECT shapes. */
 dcn_status dcn_regroup_input_f16(const dcn_shape *shape, const void *input, void *workspace,
                                  size_t workspace_bytes, dcn_stream stream);
 dcn_status dcn_forward_f16_grouped(const dcn_shape *shape, const void *input_grouped,
@@ -225,9 +231,9 @@ dcn_status dcn_prepare_offsets_f16(int64_t plane, const void *raw, const void *f
  * dcn_forward_f16, but its scratch is a fixed array inside the library
  * (dcn_static_scratch_bytes() = 16 MiB, held on every GPU that loads the
  * library until the process exits), so the caller passes only inputs and outputs.
- * Fused-path shapes only (else DCN_ERR_UNSUPPORTED); a problem whose scratch
- * exceeds the array returns DCN_ERR_SCRATCH_TOO_SMALL (16 MiB holds 7 Jasna
- * 64x64 tiles).  All calls share the array, so calls that overlap on the GPU race
+ * Tensor-core-path shapes only (else DCN_ERR_UNSUPPORTED); a problem whose
+ * scratch exceeds the array returns DCN_ERR_SCRATCH_TOO_SMALL (16 MiB holds 15
+ * Jasna 64x64 tiles on the slab path, 7 on the global-gather path).  All calls share the array, so calls that overlap on the GPU race
  * and must be ordered (one stream, or events).  The first call on a device looks
  * up the array's address; make it before any stream capture.  Allocates nothing. */
 size_t dcn_static_scratch_bytes(void);

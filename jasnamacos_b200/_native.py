@@ -33,6 +33,7 @@ DCN_WEIGHT_IC_K_OC = 1
 
 DCN_PATH_DIRECT = 0
 DCN_PATH_FUSED_TC = 1
+DCN_PATH_SLAB_TC = 2
 
 DCN_FLAG_NONFINITE = 1
 

@@ -27,6 +27,7 @@ SOURCES = [
     "dcn_api.cu",
     "dcn_direct.cu",
     "dcn_fused_sm100.cu",
+    "dcn_slab_sm100.cu",
     "dcn_prepack.cu",
     "dcn_aux.cu",
     "dcn_static_scratch.cu",

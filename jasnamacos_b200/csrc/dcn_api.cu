@@ -11,6 +11,7 @@
 
 #include <cstdlib>
 #include <mutex>
+#include <string>
 
 #include "dcn_b200.h"
 #include "dcn_common.cuh"
@@ -35,6 +36,16 @@ cudaError_t launch_regroup_c8(const Params &p, const __half *input, void *worksp
 cudaError_t launch_fused_grouped(const Params &p, const void *input_c8, const __half *offset, const __half *mask,
                                  const uint8_t *packed_w, const __half *bias, __half *output, uint32_t *flag,
                                  int sm_count, uint32_t *err, cudaStream_t stream);
+bool slab_supported(const Params &p);
+size_t slab_workspace_bytes(const Params &p);
+size_t slab_packed_weight_bytes(const Params &p);
+cudaError_t slab_prepare_device();
+cudaError_t launch_regroup_slabs(const Params &p, const __half *input, void *workspace, cudaStream_t stream);
+cudaError_t launch_prepack_slab(const Params &p, const void *src, dcn_dtype src_dtype, int layout, void *dst,
+                                cudaStream_t stream);
+cudaError_t launch_slab_grouped(const Params &p, const void *slabs, const __half *offset, const __half *mask,
+                                const uint8_t *packed_w, const __half *bias, __half *output, uint32_t *flag,
+                                int sm_count, uint32_t *err, cudaStream_t stream);
 
 namespace {
 
@@ -80,6 +91,7 @@ dcn_status current_device(DeviceInfo **out) {
         d.sm_count = sms;
         if (d.sm100) {
             e = fused_prepare_device(&d.err_word);
+            if (e == cudaSuccess) e = slab_prepare_device();
             if (e != cudaSuccess) {
                 cudaGetLastError();
                 return from_cuda(e);
@@ -125,6 +137,24 @@ dcn_status validate(const dcn_shape *s) {
     for (int64_t c : counts)
         if (c >= (int64_t{1} << 40)) return DCN_ERR_INVALID_SHAPE;
     return DCN_OK;
+}
+
+// Kernel preference for shapes both tensor-core kernels take, from the environment
+// variable DCN_B200_FUSED_KERNEL (read once): "pairs" forces the global-gather
+// kernel, "slab" or anything else keeps the default (slab where it applies).
+bool slab_allowed() {
+    static const bool allowed = [] {
+        const char *v = std::getenv("DCN_B200_FUSED_KERNEL");
+        return !(v != nullptr && std::string(v) == "pairs");
+    }();
+    return allowed;
+}
+
+// The implementation dcn_forward_f16 runs for a validated shape.
+dcn_path select_path(const Params &p) {
+    if (slab_allowed() && slab_supported(p)) return DCN_PATH_SLAB_TC;
+    if (fused_supported(p)) return DCN_PATH_FUSED_TC;
+    return DCN_PATH_DIRECT;
 }
 
 }  // namespace
@@ -218,14 +248,17 @@ dcn_status dcn_forward_f16_direct(const dcn_shape *shape, const void *input, con
 
 dcn_path dcn_forward_f16_path(const dcn_shape *shape) {
     if (validate(shape) != DCN_OK) return DCN_PATH_DIRECT;
-    return fused_supported(make_params(*shape)) ? DCN_PATH_FUSED_TC : DCN_PATH_DIRECT;
+    return select_path(make_params(*shape));
 }
 
 size_t dcn_packed_weight_bytes(const dcn_shape *shape) {
     if (validate(shape) != DCN_OK) return 0;
     const Params p = make_params(*shape);
-    if (fused_supported(p)) return static_cast<size_t>(fused_kblocks(p)) * 64 * 64 * sizeof(__half);
-    return static_cast<size_t>(p.OC) * p.cpg * p.KA * sizeof(__half);
+    switch (select_path(p)) {
+    case DCN_PATH_SLAB_TC: return slab_packed_weight_bytes(p);
+    case DCN_PATH_FUSED_TC: return static_cast<size_t>(fused_kblocks(p)) * 64 * 64 * sizeof(__half);
+    default: return static_cast<size_t>(p.OC) * p.cpg * p.KA * sizeof(__half);
+    }
 }
 
 dcn_status dcn_prepack_weights(const dcn_shape *shape, const void *weight, dcn_dtype src_dtype,
@@ -242,17 +275,47 @@ dcn_status dcn_prepack_weights(const dcn_shape *shape, const void *weight, dcn_d
     if (src_layout == DCN_WEIGHT_IC_K_OC && p.G != 1) return DCN_ERR_UNSUPPORTED;
     DeviceInfo *dev = nullptr;
     if ((st = current_device(&dev)) != DCN_OK) return st;
-    const bool fused = fused_supported(p);
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    const dcn_path path = select_path(p);
+    if (path == DCN_PATH_SLAB_TC)
+        return from_cuda(launch_prepack_slab(p, weight, src_dtype, static_cast<int>(src_layout), packed, s));
+    const bool fused = path == DCN_PATH_FUSED_TC;
     return from_cuda(launch_prepack_weights(p, fused, fused ? fused_kblocks(p) : 0, weight, src_dtype,
-                                            static_cast<int>(src_layout), packed,
-                                            reinterpret_cast<cudaStream_t>(stream)));
+                                            static_cast<int>(src_layout), packed, s));
 }
 
 size_t dcn_forward_f16_workspace_bytes(const dcn_shape *shape) {
     if (validate(shape) != DCN_OK) return 0;
     const Params p = make_params(*shape);
-    return fused_supported(p) ? fused_workspace_bytes(p) : 0;
+    switch (select_path(p)) {
+    case DCN_PATH_SLAB_TC: return slab_workspace_bytes(p);
+    case DCN_PATH_FUSED_TC: return fused_workspace_bytes(p);
+    default: return 0;
+    }
 }
+
+namespace {
+
+// The tensor-core kernel of `path` on an input already in that path's grouped layout.
+dcn_status launch_grouped(dcn_path path, const Params &p, const void *grouped, const void *offset,
+                          const void *mask, const void *packed_weight, const void *bias, void *output,
+                          uint32_t *flag, DeviceInfo *dev, cudaStream_t s) {
+    const auto *off = static_cast<const __half *>(offset);
+    const auto *msk = static_cast<const __half *>(mask);
+    const auto *w = static_cast<const uint8_t *>(packed_weight);
+    const auto *b = static_cast<const __half *>(bias);
+    auto *out = static_cast<__half *>(output);
+    if (path == DCN_PATH_SLAB_TC)
+        return from_cuda(launch_slab_grouped(p, grouped, off, msk, w, b, out, flag, dev->sm_count, dev->err_word, s));
+    return from_cuda(launch_fused_grouped(p, grouped, off, msk, w, b, out, flag, dev->sm_count, dev->err_word, s));
+}
+
+cudaError_t launch_regroup(dcn_path path, const Params &p, const void *input, void *workspace, cudaStream_t s) {
+    const auto *in = static_cast<const __half *>(input);
+    return path == DCN_PATH_SLAB_TC ? launch_regroup_slabs(p, in, workspace, s) : launch_regroup_c8(p, in, workspace, s);
+}
+
+}  // namespace
 
 dcn_status dcn_forward_f16(const dcn_shape *shape, const void *input, const void *offset, const void *mask,
                            const void *packed_weight, const void *bias, void *output, uint32_t *nonfinite_flag,
@@ -267,7 +330,8 @@ dcn_status dcn_forward_f16(const dcn_shape *shape, const void *input, const void
     if ((st = current_device(&dev)) != DCN_OK) return st;
     const Params p = make_params(*shape);
     cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-    if (!fused_supported(p)) {
+    const dcn_path path = select_path(p);
+    if (path == DCN_PATH_DIRECT) {
         if (!aligned(offset, 2) || !aligned(mask, 2)) return DCN_ERR_INVALID_ARGUMENT;
         cudaError_t e = launch_direct_f16(p, static_cast<const __half *>(input),
                                           static_cast<const __half *>(offset), static_cast<const __half *>(mask),
@@ -279,18 +343,14 @@ dcn_status dcn_forward_f16(const dcn_shape *shape, const void *input, const void
                                        dev->sm_count, s);
         return from_cuda(e);
     }
-    // Fused path: offsets/masks are read by TMA (16-byte aligned rows), the
-    // regrouped input by 16-byte loads.
+    // Tensor-core paths: offsets/masks are read by TMA (16-byte aligned rows), the
+    // regrouped input by 16/32-byte loads.
     if (!aligned(offset, 16) || !aligned(mask, 16)) return DCN_ERR_INVALID_ARGUMENT;
-    if (!workspace || !aligned(workspace, 256) || workspace_bytes < fused_workspace_bytes(p))
+    if (!workspace || !aligned(workspace, 256) || workspace_bytes < dcn_forward_f16_workspace_bytes(shape))
         return DCN_ERR_INVALID_ARGUMENT;
-    cudaError_t e = launch_regroup_c8(p, static_cast<const __half *>(input), workspace, s);
+    cudaError_t e = launch_regroup(path, p, input, workspace, s);
     if (e != cudaSuccess) return from_cuda(e);
-    return from_cuda(launch_fused_grouped(p, workspace, static_cast<const __half *>(offset),
-                                          static_cast<const __half *>(mask),
-                                          static_cast<const uint8_t *>(packed_weight),
-                                          static_cast<const __half *>(bias), static_cast<__half *>(output),
-                                          nonfinite_flag, dev->sm_count, dev->err_word, s));
+    return launch_grouped(path, p, workspace, offset, mask, packed_weight, bias, output, nonfinite_flag, dev, s);
 }
 
 dcn_status dcn_regroup_input_f16(const dcn_shape *shape, const void *input, void *workspace,
@@ -298,14 +358,14 @@ dcn_status dcn_regroup_input_f16(const dcn_shape *shape, const void *input, void
     dcn_status st = validate(shape);
     if (st != DCN_OK) return st;
     const Params p = make_params(*shape);
-    if (!fused_supported(p)) return DCN_ERR_UNSUPPORTED;
+    const dcn_path path = select_path(p);
+    if (path == DCN_PATH_DIRECT) return DCN_ERR_UNSUPPORTED;
     if (!input || !workspace || !aligned(input, 2) || !aligned(workspace, 256) ||
-        workspace_bytes < fused_workspace_bytes(p))
+        workspace_bytes < dcn_forward_f16_workspace_bytes(shape))
         return DCN_ERR_INVALID_ARGUMENT;
     DeviceInfo *dev = nullptr;
     if ((st = current_device(&dev)) != DCN_OK) return st;
-    return from_cuda(launch_regroup_c8(p, static_cast<const __half *>(input), workspace,
-                                       reinterpret_cast<cudaStream_t>(stream)));
+    return from_cuda(launch_regroup(path, p, input, workspace, reinterpret_cast<cudaStream_t>(stream)));
 }
 
 dcn_status dcn_forward_f16_grouped(const dcn_shape *shape, const void *input_grouped, const void *offset,
@@ -314,19 +374,16 @@ dcn_status dcn_forward_f16_grouped(const dcn_shape *shape, const void *input_gro
     dcn_status st = validate(shape);
     if (st != DCN_OK) return st;
     const Params p = make_params(*shape);
-    if (!fused_supported(p)) return DCN_ERR_UNSUPPORTED;
+    const dcn_path path = select_path(p);
+    if (path == DCN_PATH_DIRECT) return DCN_ERR_UNSUPPORTED;
     if (!input_grouped || !offset || !mask || !packed_weight || !bias || !output) return DCN_ERR_INVALID_ARGUMENT;
     if (!aligned(input_grouped, 16) || !aligned(offset, 16) || !aligned(mask, 16) || !aligned(packed_weight, 16) ||
         !aligned(bias, 2) || !aligned(output, 2) || (nonfinite_flag && !aligned(nonfinite_flag, 4)))
         return DCN_ERR_INVALID_ARGUMENT;
     DeviceInfo *dev = nullptr;
     if ((st = current_device(&dev)) != DCN_OK) return st;
-    return from_cuda(launch_fused_grouped(p, input_grouped, static_cast<const __half *>(offset),
-                                          static_cast<const __half *>(mask),
-                                          static_cast<const uint8_t *>(packed_weight),
-                                          static_cast<const __half *>(bias), static_cast<__half *>(output),
-                                          nonfinite_flag, dev->sm_count, dev->err_word,
-                                          reinterpret_cast<cudaStream_t>(stream)));
+    return launch_grouped(path, p, input_grouped, offset, mask, packed_weight, bias, output, nonfinite_flag, dev,
+                          reinterpret_cast<cudaStream_t>(stream));
 }
 
 dcn_status dcn_flag_non_finite_f16(const void *values, int64_t count, uint32_t *flag, dcn_stream stream) {

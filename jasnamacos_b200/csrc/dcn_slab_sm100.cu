@@ -1,0 +1,587 @@
+// dcn_slab_sm100.cu -- fused FP16 DCNv2 for small images (the 64x64 tiles of the
+// Jasna restoration pipeline): every deformable group's input is staged whole in
+// shared memory and gathered from there.
+//
+// Same operator as dcn_fused_sm100.cu (bilinear sample * mask -> FP16 A operand in
+// tensor memory -> tcgen05.mma against the weights -> bias, FP16, NCHW, Inf/NaN
+// flag), organised for images whose per-group input plane fits in shared memory:
+//
+//   work unit = up to 4 consecutive 128-pixel tiles of one image (4 accumulators,
+//               64 TMEM columns each, live across all deformable groups)
+//   for each deformable group g (16 for Jasna):
+//       the loader bulk-copies the group's zero-bordered input slab
+//       ([H+2][W+2] x 8 channels FP16, 69,696 B for 64x64) and the group's slice
+//       of the weights (5 K=16 blocks, 10 KB) into one of two shared buffers
+//       for each tile of the unit:
+//           the loader TMA-loads the tile's 18 offset and 9 mask rows of group g
+//           12 producer warps sample the 9 taps (3 each) from the slab with
+//           16-byte shared loads and store 9 chunks (+1 zero chunk) of A in TMEM
+//           the MMA thread issues 5 MMAs (K = 80) into the tile's accumulator
+//   4 epilogue warps drain each tile's accumulator after its last group.
+//
+// Compared with gathering from global memory this trades the random 32-byte L1
+// requests (one data-pipe wavefront per lane, ~500 cycles) for random 16-byte
+// shared loads (~2.5 wavefronts per 8 lanes, ~30 cycles), and reads each input
+// byte from L2 once per work unit instead of once per sample.
+//
+// Every mbarrier wait is bounded (kWaitLimitNs); a timeout sets the device error
+// word, stops the CTA's warps, drains in-flight copies and MMAs and frees TMEM.
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <cudaTypedefs.h>
+
+#include "dcn_common.cuh"
+
+namespace dcn {
+
+namespace slab {
+
+constexpr int BM = 128;              // pixels per tile
+constexpr int BN = 64;               // output channels
+constexpr int kMaxTilesPerUnit = 4;  // accumulators kept in TMEM
+constexpr int kTaps = 9;             // 3x3
+constexpr int kChunks = 10;          // 9 taps + 1 zero chunk -> K = 80 = 5 MMAs of K = 16
+constexpr int kMmasPerStage = kChunks / 2;
+constexpr int kBBlockBytes = BN * 32;                     // one K=16 block, SW32 K-major: 64 rows x 32 B
+constexpr int kBGroupBytes = kMmasPerStage * kBBlockBytes;  // 10 KB per deformable group
+constexpr int kStages = 4;                                // (tile, group) stages in flight
+constexpr int kOffRows = 2 * kTaps;                       // 18 offset rows per (tile, group)
+constexpr int kMaskRows = kTaps;                          // 9 mask rows
+constexpr uint32_t kStageTxBytes = (kOffRows + kMaskRows) * BM * 2;
+constexpr int kProducerWarps = 12;  // 3 per TMEM lane quarter, 3 taps each
+constexpr int kEpilogueWarps = 4;
+constexpr int kThreads = (4 + kEpilogueWarps + kProducerWarps) * 32;  // 640
+constexpr uint32_t kTmemCols = 512;
+constexpr uint32_t kACol0 = kMaxTilesPerUnit * BN;  // 256: A stages after the accumulators
+constexpr uint32_t kAStageCols = kChunks * 4;       // 40 columns per stage
+constexpr uint32_t kIdleBackoffNs = 200;
+constexpr int kMaxSlabBytes = 88 * 1024;            // two slabs + ~49 KB of fixed buffers fit 227 KB
+
+// Shared memory: fixed part; the two slabs follow it (size depends on H, W).
+struct __align__(1024) Smem {
+    uint8_t b[2][kBGroupBytes];           // weight slices of the two buffered groups (256-aligned)
+    __half off[kStages][kOffRows][BM];    // TMA boxes
+    __half msk[kStages][kMaskRows][BM];
+    float bias[BN];
+    int2 tap[kTaps];                      // {ky*DH, kx*DW}
+    uint64_t grp_full[2];                 // slab + weights of a group landed
+    uint64_t grp_empty[2];                // producers done with the slab, MMAs done with the weights
+    uint64_t om_full[kStages];
+    uint64_t om_empty[kStages];
+    uint64_t a_full[kStages];
+    uint64_t a_empty[kStages];
+    uint64_t acc_full[kMaxTilesPerUnit];
+    uint64_t acc_empty[kMaxTilesPerUnit];
+    uint32_t tmem_base;
+    int abort_flag;
+};
+
+struct Args {
+    Params p;
+    const uint8_t *slabs;      // [N][OG][H+2][W+2][8] FP16 (zero border), see regroup_slabs_kernel
+    const uint8_t *packed_w;   // OG * kBGroupBytes, SW32 K-major blocks
+    const __half *bias;
+    __half *out;
+    uint32_t *flag;
+    uint32_t *err;
+    int slab_bytes;            // (H+2)(W+2)*16
+    int tiles_per_image;
+    int tiles_per_unit;        // 1..4
+    int units_per_image;
+    int num_units;
+};
+
+__device__ __forceinline__ uint32_t pack_half2(__half2 h) { return *reinterpret_cast<uint32_t *>(&h); }
+
+__device__ __forceinline__ void signal_abort(Smem &s, uint32_t *err) {
+    s.abort_flag = 1;
+    atomicOr(err, kErrWaitTimeout);
+}
+
+__device__ __forceinline__ uint4 lds128(uint32_t addr) {
+    uint4 v;
+    asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(addr));
+    return v;
+}
+
+// Shared-memory descriptor of one K=16 slice of B stored K-major with the 32-byte
+// swizzle: rows of 32 bytes, 8-row (256-byte) atoms; layout code 6 = SWIZZLE_32B.
+__device__ __forceinline__ uint64_t make_sw32_kmajor_desc(uint32_t smem_byte_addr) {
+    uint64_t d = 0;
+    d |= static_cast<uint64_t>((smem_byte_addr >> 4) & 0x3FFFu);
+    d |= static_cast<uint64_t>(1u) << 16;
+    d |= static_cast<uint64_t>(256u >> 4) << 32;
+    d |= static_cast<uint64_t>(1u) << 46;
+    d |= static_cast<uint64_t>(6u) << 61;
+    return d;
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+    slab_dcn_kernel(const __grid_constant__ CUtensorMap tmap_off, const __grid_constant__ CUtensorMap tmap_msk,
+                    const Args a) {
+    extern __shared__ uint8_t smem_raw[];
+    Smem &s = *reinterpret_cast<Smem *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t{1023});
+    uint8_t *slab_base = reinterpret_cast<uint8_t *>(&s) + ((sizeof(Smem) + 127) & ~size_t{127});
+    const int warp = threadIdx.x / 32;
+    const int lane = threadIdx.x % 32;
+    const Params &p = a.p;
+    volatile int *abort_flag = &s.abort_flag;
+    const int slab_stride = (a.slab_bytes + 127) & ~127;
+
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(&s.grp_full[i], 1);
+            mbar_init(&s.grp_empty[i], kProducerWarps + 1);
+        }
+        for (int i = 0; i < kStages; ++i) {
+            mbar_init(&s.om_full[i], 1);
+            mbar_init(&s.om_empty[i], kProducerWarps);
+            mbar_init(&s.a_full[i], kProducerWarps);
+            mbar_init(&s.a_empty[i], 1);
+        }
+        for (int i = 0; i < kMaxTilesPerUnit; ++i) {
+            mbar_init(&s.acc_full[i], 1);
+            mbar_init(&s.acc_empty[i], kEpilogueWarps);
+        }
+        s.abort_flag = 0;
+        fence_mbarrier_init();
+    }
+    if (threadIdx.x < BN) s.bias[threadIdx.x] = __half2float(a.bias[threadIdx.x]);
+    if (threadIdx.x < kTaps) {
+        const int ky = threadIdx.x / p.KW;
+        s.tap[threadIdx.x] = make_int2(ky * p.DH, (static_cast<int>(threadIdx.x) - ky * p.KW) * p.DW);
+    }
+    if (warp == 1) {
+        tmem_alloc(&s.tmem_base, kTmemCols);
+        tmem_relinquish();
+    }
+    if (warp == 0 && lane == 0) {
+        prefetch_tensor_map(&tmap_off);
+        prefetch_tensor_map(&tmap_msk);
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = s.tmem_base;
+
+    // The zero chunk (K columns 72..79) of every A stage is written once here and
+    // never again; the producers only store chunks 0..8.
+    if (warp >= 8 && warp < 12) {
+        const uint32_t lane_base = tmem + (static_cast<uint32_t>((warp % 4) * 32) << 16);
+        for (int st = 0; st < kStages; ++st)
+            tmem_st_32x32b_x4(lane_base + kACol0 + st * kAStageCols + kTaps * 4, 0u, 0u, 0u, 0u);
+        tmem_wait_st();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+
+    const int OG = p.OG;
+    if (warp == 0) {
+        // ------------------------------------------------------------ loader
+        if (lane == 0) {
+            uint32_t gi = 0, si = 0;
+            bool ok = true;
+            for (int u = blockIdx.x; u < a.num_units && ok; u += gridDim.x) {
+                const int n = u / a.units_per_image;
+                const int t0 = (u % a.units_per_image) * a.tiles_per_unit;
+                const int mt = min(a.tiles_per_unit, a.tiles_per_image - t0);
+                for (int g = 0; g < OG && ok; ++g, ++gi) {
+                    const uint32_t gb = gi & 1u, gph = (gi >> 1) & 1u;
+                    if (!mbar_wait_bounded(&s.grp_empty[gb], gph ^ 1u, abort_flag)) {
+                        signal_abort(s, a.err);
+                        ok = false;
+                        break;
+                    }
+                    mbar_arrive_expect_tx(&s.grp_full[gb], static_cast<uint32_t>(a.slab_bytes + kBGroupBytes));
+                    const uint8_t *src = a.slabs + (static_cast<size_t>(n) * OG + g) * a.slab_bytes;
+                    uint8_t *dst = slab_base + gb * slab_stride;
+                    for (int off = 0; off < a.slab_bytes; off += 32768) {
+                        const int bytes = min(32768, a.slab_bytes - off);
+                        bulk_copy_g2s(dst + off, src + off, static_cast<uint32_t>(bytes), &s.grp_full[gb]);
+                    }
+                    bulk_copy_g2s(s.b[gb], a.packed_w + static_cast<size_t>(g) * kBGroupBytes, kBGroupBytes,
+                                  &s.grp_full[gb]);
+                    for (int t = 0; t < mt; ++t, ++si) {
+                        const uint32_t st = si % kStages, ph = (si / kStages) & 1u;
+                        if (!mbar_wait_bounded(&s.om_empty[st], ph ^ 1u, abort_flag)) {
+                            signal_abort(s, a.err);
+                            ok = false;
+                            break;
+                        }
+                        mbar_arrive_expect_tx(&s.om_full[st], kStageTxBytes);
+                        const int px0 = (t0 + t) * BM;
+                        tma_load_3d(&s.off[st][0][0], &tmap_off, &s.om_full[st], px0, kOffRows * g, n);
+                        tma_load_3d(&s.msk[st][0][0], &tmap_msk, &s.om_full[st], px0, kMaskRows * g, n);
+                    }
+                }
+            }
+            // Drain every copy issued before leaving.
+            for (uint32_t k = 0; k < 2 && k < gi; ++k) {
+                const uint32_t last = gi - 1 - k;
+                mbar_wait_bounded(&s.grp_full[last & 1u], (last >> 1) & 1u, nullptr);
+            }
+            for (uint32_t k = 0; k < kStages && k < si; ++k) {
+                const uint32_t last = si - 1 - k;
+                mbar_wait_bounded(&s.om_full[last % kStages], (last / kStages) & 1u, nullptr);
+            }
+        }
+    } else if (warp == 1) {
+        // --------------------------------------------------------------- MMA
+        if (lane == 0) {
+            const uint32_t idesc = make_idesc_f16_f32(BM, BN);
+            uint32_t gi = 0, si = 0;
+            uint32_t uses[kMaxTilesPerUnit] = {0, 0, 0, 0};
+            uint64_t *last_bar = nullptr;
+            uint32_t last_parity = 0;
+            bool ok = true;
+            for (int u = blockIdx.x; u < a.num_units && ok; u += gridDim.x) {
+                const int t0 = (u % a.units_per_image) * a.tiles_per_unit;
+                const int mt = min(a.tiles_per_unit, a.tiles_per_image - t0);
+                for (int g = 0; g < OG && ok; ++g, ++gi) {
+                    const uint32_t gb = gi & 1u, gph = (gi >> 1) & 1u;
+                    if (!mbar_wait_bounded(&s.grp_full[gb], gph, abort_flag)) {
+                        signal_abort(s, a.err);
+                        ok = false;
+                        break;
+                    }
+                    const uint32_t b_base = smem_addr(s.b[gb]);
+                    for (int t = 0; t < mt; ++t, ++si) {
+                        if (g == 0) {
+                            if (!mbar_wait_bounded(&s.acc_empty[t], (uses[t] & 1u) ^ 1u, abort_flag)) {
+                                signal_abort(s, a.err);
+                                ok = false;
+                                break;
+                            }
+                        }
+                        const uint32_t st = si % kStages, ph = (si / kStages) & 1u;
+                        if (!mbar_wait_bounded(&s.a_full[st], ph, abort_flag)) {
+                            signal_abort(s, a.err);
+                            ok = false;
+                            break;
+                        }
+                        tc_fence_after();
+                        const uint32_t d_tmem = tmem + t * BN;
+                        const uint32_t a_tmem = tmem + kACol0 + st * kAStageCols;
+#pragma unroll
+                        for (int kk = 0; kk < kMmasPerStage; ++kk) {
+                            const uint64_t bdesc = make_sw32_kmajor_desc(b_base + kk * kBBlockBytes);
+                            umma_f16_ts(d_tmem, a_tmem + kk * 8, bdesc, idesc, (g | kk) != 0 ? 1u : 0u);
+                        }
+                        umma_commit(&s.a_empty[st]);
+                        last_bar = &s.a_empty[st];
+                        last_parity = ph;
+                        if (g == OG - 1) {
+                            umma_commit(&s.acc_full[t]);
+                            last_bar = &s.acc_full[t];
+                            last_parity = uses[t] & 1u;
+                            ++uses[t];
+                        }
+                    }
+                    if (!ok) break;
+                    umma_commit(&s.grp_empty[gb]);  // the weights of this group are no longer read
+                }
+            }
+            if (last_bar != nullptr) mbar_wait_bounded(last_bar, last_parity, nullptr);
+        }
+    } else if (warp < 4) {
+        // warps 2-3: no role
+    } else if (warp < 8) {
+        // ---------------------------------------------------------- epilogue
+        const int q = warp % 4;
+        const int r = q * 32 + lane;
+        uint32_t uses[kMaxTilesPerUnit] = {0, 0, 0, 0};
+        bool nonfinite = false;
+        bool ok = true;
+        for (int u = blockIdx.x; u < a.num_units && ok; u += gridDim.x) {
+            const int n = u / a.units_per_image;
+            const int t0 = (u % a.units_per_image) * a.tiles_per_unit;
+            const int mt = min(a.tiles_per_unit, a.tiles_per_image - t0);
+            for (int t = 0; t < mt; ++t) {
+                if (!mbar_wait_bounded(&s.acc_full[t], uses[t] & 1u, abort_flag, kIdleBackoffNs)) {
+                    signal_abort(s, a.err);
+                    ok = false;
+                    break;
+                }
+                ++uses[t];
+                tc_fence_after();
+                uint32_t v[BN];
+                const uint32_t taddr = tmem + (static_cast<uint32_t>(q * 32) << 16) + t * BN;
+#pragma unroll
+                for (int c = 0; c < BN; c += 16) tmem_ld_32x32b_x16(taddr + c, &v[c]);
+                tmem_wait_ld();
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&s.acc_empty[t]);
+                const int px = (t0 + t) * BM + r;
+                if (px < p.out_plane) {
+                    __half *dst = a.out + static_cast<size_t>(n) * BN * p.out_plane + px;
+#pragma unroll
+                    for (int oc = 0; oc < BN; ++oc) {
+                        const __half h = __float2half_rn(__uint_as_float(v[oc]) + s.bias[oc]);
+                        nonfinite |= __hisinf(h) != 0 || __hisnan(h);
+                        dst[static_cast<size_t>(oc) * p.out_plane] = h;
+                    }
+                }
+            }
+        }
+        if (a.flag != nullptr && __any_sync(0xffffffffu, nonfinite) && lane == 0)
+            atomicOr(a.flag, DCN_FLAG_NONFINITE);
+    } else {
+        // --------------------------------------------------------- producers
+        const int pw = warp - 8;       // 0..11
+        const int q = warp % 4;        // TMEM lane quarter
+        const int tap0 = (pw / 4) * 3;  // taps tap0..tap0+2
+        const int r = q * 32 + lane;
+        const uint32_t lane_base = tmem + (static_cast<uint32_t>(q * 32) << 16);
+        const int sw = p.W + 2;  // slab row stride in positions
+        const uint32_t slab0 = smem_addr(slab_base);
+        uint32_t gi = 0, si = 0;
+        bool ok = true;
+        for (int u = blockIdx.x; u < a.num_units && ok; u += gridDim.x) {
+            const int t0 = (u % a.units_per_image) * a.tiles_per_unit;
+            const int mt = min(a.tiles_per_unit, a.tiles_per_image - t0);
+            for (int g = 0; g < OG && ok; ++g, ++gi) {
+                const uint32_t gb = gi & 1u, gph = (gi >> 1) & 1u;
+                if (!mbar_wait_bounded(&s.grp_full[gb], gph, abort_flag)) {
+                    ok = false;
+                    break;
+                }
+                const uint32_t slab = slab0 + gb * slab_stride;
+                for (int t = 0; t < mt; ++t, ++si) {
+                    const uint32_t st = si % kStages, ph = (si / kStages) & 1u;
+                    const int px = (t0 + t) * BM + r;
+                    const bool valid = px < p.out_plane;
+                    const int oy = valid ? px / p.WO : 0;
+                    const int ox = valid ? px - oy * p.WO : 0;
+                    if (!mbar_wait_bounded(&s.om_full[st], ph, abort_flag)) {
+                        ok = false;
+                        break;
+                    }
+                    float fy[3], fx[3], m[3];
+                    uint32_t base_addr[3];
+                    bool in[3];
+#pragma unroll
+                    for (int i = 0; i < 3; ++i) {
+                        const int k = tap0 + i;
+                        const int2 tk = s.tap[k];
+                        const float y = static_cast<float>(oy * p.SH - p.PH + tk.x) + __half2float(s.off[st][2 * k][r]);
+                        const float x = static_cast<float>(ox * p.SW - p.PW + tk.y) + __half2float(s.off[st][2 * k + 1][r]);
+                        m[i] = __half2float(s.msk[st][k][r]);
+                        const int y0 = __float2int_rd(y);
+                        const int x0 = __float2int_rd(x);
+                        fy[i] = y - static_cast<float>(y0);
+                        fx[i] = x - static_cast<float>(x0);
+                        // Padded slab: rows/columns -1 and H/W are zeros, so a sample is
+                        // either fully inside [-1, H-1] x [-1, W-1] or contributes zero.
+                        in[i] = valid && static_cast<unsigned>(y0 + 1) <= static_cast<unsigned>(p.H) &&
+                                static_cast<unsigned>(x0 + 1) <= static_cast<unsigned>(p.W);
+                        base_addr[i] = slab + static_cast<uint32_t>(((y0 + 1) * sw + (x0 + 1)) * 16);
+                    }
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&s.om_empty[st]);
+
+                    uint32_t outw[3][4];
+#pragma unroll
+                    for (int i = 0; i < 3; ++i) {
+                        uint4 c00 = make_uint4(0u, 0u, 0u, 0u), c01 = c00, c10 = c00, c11 = c00;
+                        if (in[i]) {
+                            c00 = lds128(base_addr[i]);
+                            c01 = lds128(base_addr[i] + 16);
+                            c10 = lds128(base_addr[i] + sw * 16);
+                            c11 = lds128(base_addr[i] + sw * 16 + 16);
+                        }
+                        const float mhy = m[i] * (1.0f - fy[i]);
+                        const float mly = m[i] * fy[i];
+                        const __half2 w00 = __float2half2_rn(mhy * (1.0f - fx[i]));
+                        const __half2 w01 = __float2half2_rn(mhy * fx[i]);
+                        const __half2 w10 = __float2half2_rn(mly * (1.0f - fx[i]));
+                        const __half2 w11 = __float2half2_rn(mly * fx[i]);
+                        const __half2 *h00 = reinterpret_cast<const __half2 *>(&c00);
+                        const __half2 *h01 = reinterpret_cast<const __half2 *>(&c01);
+                        const __half2 *h10 = reinterpret_cast<const __half2 *>(&c10);
+                        const __half2 *h11 = reinterpret_cast<const __half2 *>(&c11);
+#pragma unroll
+                        for (int e = 0; e < 4; ++e) {
+                            __half2 acc = __hmul2(w00, h00[e]);
+                            acc = __hfma2(w01, h01[e], acc);
+                            acc = __hfma2(w10, h10[e], acc);
+                            acc = __hfma2(w11, h11[e], acc);
+                            outw[i][e] = pack_half2(acc);
+                        }
+                    }
+                    if (!mbar_wait_bounded(&s.a_empty[st], ph ^ 1u, abort_flag)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+#pragma unroll
+                    for (int i = 0; i < 3; ++i)
+                        tmem_st_32x32b_x4(lane_base + kACol0 + st * kAStageCols + (tap0 + i) * 4, outw[i][0],
+                                          outw[i][1], outw[i][2], outw[i][3]);
+                    tmem_wait_st();
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&s.a_full[st]);
+                }
+                if (!ok) break;
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&s.grp_empty[gb]);  // done reading this slab
+            }
+        }
+        if (!ok) signal_abort(s, a.err);
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (warp == 1) tmem_dealloc(tmem, kTmemCols);
+}
+
+// NCHW FP16 -> zero-bordered slabs [N][C/8][H+2][W+2][8]: slab (n, g) holds the 8
+// channels of deformable group g at every position, 16 bytes per position, with a
+// one-pixel ring of zeros so bilinear corners just outside the image read zero.
+__global__ void __launch_bounds__(256) regroup_slabs_kernel(const __half *__restrict__ in, uint4 *__restrict__ out,
+                                                             int C, int H, int W, int64_t total) {
+    const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;  // padded position index
+    if (i >= total) return;
+    const int sw = W + 2;
+    const int px = static_cast<int>(i % sw);
+    const int64_t rest = i / sw;
+    const int py = static_cast<int>(rest % (H + 2));
+    const int64_t ng = rest / (H + 2);  // n * (C/8) + g
+    const int y = py - 1, x = px - 1;
+    uint4 o = make_uint4(0u, 0u, 0u, 0u);
+    if (y >= 0 && y < H && x >= 0 && x < W) {
+        const int64_t plane = static_cast<int64_t>(H) * W;
+        const __half *src = in + ng * 8 * plane + static_cast<int64_t>(y) * W + x;
+        __half h[8];
+#pragma unroll
+        for (int c = 0; c < 8; ++c) h[c] = src[c * plane];
+        o.x = pack_half2(__halves2half2(h[0], h[1]));
+        o.y = pack_half2(__halves2half2(h[2], h[3]));
+        o.z = pack_half2(__halves2half2(h[4], h[5]));
+        o.w = pack_half2(__halves2half2(h[6], h[7]));
+    }
+    out[i] = o;
+}
+
+// Weights -> per-group SW32 K-major B blocks.  Group g, block kk (K = 16: taps 2kk,
+// 2kk+1 x 8 channels), output channel row n (0..63), 16-byte physical chunk pc:
+// logical chunk c = pc ^ ((n >> 2) & 1), tap = 2kk + c (tap 9 is zero), channel
+// ic = 8g + e.  Byte ((g*5 + kk)*64 + n)*32 + pc*16 + 2e.
+template <typename T>
+__global__ void prepack_slab_kernel(const T *__restrict__ src, int layout, __half *__restrict__ dst, int OG, int cpg,
+                                    int KA, int OC) {
+    const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;  // destination half
+    const int64_t total = static_cast<int64_t>(OG) * kBGroupBytes / 2;
+    if (i >= total) return;
+    const int e = static_cast<int>(i % 8);
+    const int pc = static_cast<int>((i / 8) % 2);
+    const int n = static_cast<int>((i / 16) % 64);
+    const int kk = static_cast<int>((i / (16 * 64)) % kMmasPerStage);
+    const int g = static_cast<int>(i / (16 * 64 * kMmasPerStage));
+    const int c = pc ^ ((n >> 2) & 1);
+    const int tap = 2 * kk + c;
+    float v = 0.0f;
+    if (tap < kTaps) {
+        const int ic = g * 8 + e;
+        const int64_t idx = layout == DCN_WEIGHT_OIHW ? (static_cast<int64_t>(n) * cpg + ic) * KA + tap
+                                                      : (static_cast<int64_t>(ic) * KA + tap) * OC + n;
+        v = static_cast<float>(src[idx]);
+    }
+    dst[i] = __float2half_rn(v);
+}
+
+}  // namespace slab
+
+// Shapes the slab kernel takes: the fused-kernel class (1 conv group, 64 output
+// channels, 8 channels per deformable group) with a 3x3 kernel, an output plane
+// that is a multiple of 8 pixels, and a per-group input slab that fits twice in
+// shared memory next to the fixed buffers.
+bool slab_supported(const Params &p) {
+    if (p.G != 1 || p.OC != slab::BN || p.cpog != 8 || p.KH != 3 || p.KW != 3) return false;
+    if (p.out_plane % 8 != 0) return false;
+    const int64_t slab_bytes = static_cast<int64_t>(p.H + 2) * (p.W + 2) * 16;
+    if (slab_bytes > slab::kMaxSlabBytes) return false;
+    if (static_cast<int64_t>(p.N) * p.OG * slab_bytes >= (int64_t{1} << 40)) return false;
+    return true;
+}
+
+size_t slab_workspace_bytes(const Params &p) {
+    const size_t bytes = static_cast<size_t>(p.N) * p.OG * (p.H + 2) * (p.W + 2) * 16;
+    return (bytes + 255) & ~size_t{255};
+}
+
+size_t slab_packed_weight_bytes(const Params &p) { return static_cast<size_t>(p.OG) * slab::kBGroupBytes; }
+
+size_t slab_smem_bytes(const Params &p) {
+    const int slab_bytes = (p.H + 2) * (p.W + 2) * 16;
+    return 1024 + ((sizeof(slab::Smem) + 127) & ~size_t{127}) + 2 * static_cast<size_t>((slab_bytes + 127) & ~127);
+}
+
+cudaError_t slab_prepare_device() {
+    // Opt in to the largest dynamic shared memory any supported shape needs.
+    const int max_slab = (slab::kMaxSlabBytes + 127) & ~127;
+    const size_t smem = 1024 + ((sizeof(slab::Smem) + 127) & ~size_t{127}) + 2 * static_cast<size_t>(max_slab);
+    return cudaFuncSetAttribute(slab::slab_dcn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                static_cast<int>(smem));
+}
+
+cudaError_t launch_regroup_slabs(const Params &p, const __half *input, void *workspace, cudaStream_t stream) {
+    const int64_t total = static_cast<int64_t>(p.N) * (p.C / 8) * (p.H + 2) * (p.W + 2);
+    slab::regroup_slabs_kernel<<<static_cast<unsigned>((total + 255) / 256), 256, 0, stream>>>(
+        input, static_cast<uint4 *>(workspace), p.C, p.H, p.W, total);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_prepack_slab(const Params &p, const void *src, dcn_dtype src_dtype, int layout, void *dst,
+                                cudaStream_t stream) {
+    const int64_t total = static_cast<int64_t>(p.OG) * slab::kBGroupBytes / 2;
+    const unsigned blocks = static_cast<unsigned>((total + 255) / 256);
+    if (src_dtype == DCN_DTYPE_F32)
+        slab::prepack_slab_kernel<float><<<blocks, 256, 0, stream>>>(static_cast<const float *>(src), layout,
+                                                                     static_cast<__half *>(dst), p.OG, p.cpg,
+                                                                     p.KA, p.OC);
+    else
+        slab::prepack_slab_kernel<__half><<<blocks, 256, 0, stream>>>(static_cast<const __half *>(src), layout,
+                                                                      static_cast<__half *>(dst), p.OG, p.cpg,
+                                                                      p.KA, p.OC);
+    return cudaGetLastError();
+}
+
+namespace fused {
+bool make_plane_map(CUtensorMap *map, const void *base, int64_t plane, int channels, int batch, int rows);
+}
+
+cudaError_t launch_slab_grouped(const Params &p, const void *slabs, const __half *offset, const __half *mask,
+                                const uint8_t *packed_w, const __half *bias, __half *output, uint32_t *flag,
+                                int sm_count, uint32_t *err, cudaStream_t stream) {
+    using namespace slab;
+    CUtensorMap tmap_off, tmap_msk;
+    if (!fused::make_plane_map(&tmap_off, offset, p.out_plane, 2 * p.OG * p.KA, p.N, kOffRows) ||
+        !fused::make_plane_map(&tmap_msk, mask, p.out_plane, p.OG * p.KA, p.N, kMaskRows))
+        return cudaErrorInvalidValue;
+    Args a;
+    a.p = p;
+    a.slabs = static_cast<const uint8_t *>(slabs);
+    a.packed_w = packed_w;
+    a.bias = bias;
+    a.out = output;
+    a.flag = flag;
+    a.err = err;
+    a.slab_bytes = (p.H + 2) * (p.W + 2) * 16;
+    a.tiles_per_image = (p.out_plane + BM - 1) / BM;
+    // Up to 4 tiles per work unit (each unit reads every group's slab once); fewer
+    // when that would leave SMs idle.
+    int tpu = kMaxTilesPerUnit;
+    while (tpu > 1 && static_cast<int64_t>(p.N) * ((a.tiles_per_image + tpu - 1) / tpu) < 2 * sm_count) tpu /= 2;
+    a.tiles_per_unit = tpu;
+    a.units_per_image = (a.tiles_per_image + tpu - 1) / tpu;
+    a.num_units = p.N * a.units_per_image;
+    const int grid = a.num_units < sm_count ? a.num_units : sm_count;
+    slab_dcn_kernel<<<grid, kThreads, slab_smem_bytes(p), stream>>>(tmap_off, tmap_msk, a);
+    return cudaGetLastError();
+}
+
+}  // namespace dcn

@@ -13,7 +13,7 @@
 //  * every GPU that loads this library holds kStaticScratchBytes (16 MiB) for the
 //    life of the process;
 //  * problems whose scratch would exceed that are rejected with
-//    DCN_ERR_SCRATCH_TOO_SMALL (16 MiB holds 7 Jasna 64x64 tiles per call);
+//    DCN_ERR_SCRATCH_TOO_SMALL (16 MiB holds 15 Jasna 64x64 tiles per call on the slab path, 7 on the global-gather path);
 //  * all calls share the one array: two calls that overlap on the GPU (different
 //    streams, no ordering between them) race on it and give wrong results;
 //  * the first call on a device looks up the array's device address
@@ -69,7 +69,7 @@ extern "C" dcn_status dcn_forward_f16_static_scratch(const dcn_shape *shape, con
                                                      dcn_stream stream) {
     dcn_status st = dcn_shape_validate(shape);
     if (st != DCN_OK) return st;
-    if (dcn_forward_f16_path(shape) != DCN_PATH_FUSED_TC) return DCN_ERR_UNSUPPORTED;
+    if (dcn_forward_f16_path(shape) == DCN_PATH_DIRECT) return DCN_ERR_UNSUPPORTED;
     const size_t need = dcn_forward_f16_workspace_bytes(shape);
     if (need > kStaticScratchBytes) return DCN_ERR_SCRATCH_TOO_SMALL;
     void *scratch = nullptr;

@@ -46,7 +46,7 @@ def test_library_is_self_contained():
 
 def test_abi_version_and_status_strings(lib):
     assert lib.dcn_abi_version() == 1
-    for code in range(9):
+    for code in range(10):
         assert lib.dcn_status_string(code)
     assert lib.dcn_status_is_recoverable(_native.DCN_ERR_NONFINITE) == 1
     for code in (0, 1, 2, 3, 4, 6, 7, 8):
@@ -75,10 +75,16 @@ def test_check_counts(lib):
 
 def test_path_selection_and_sizes(lib):
     jasna = DeformConvShape.jasna_propagation().to_c()
-    assert lib.dcn_forward_f16_path(ctypes.byref(jasna)) == _native.DCN_PATH_FUSED_TC
-    assert lib.dcn_packed_weight_bytes(ctypes.byref(jasna)) == 18 * 8192
-    # corner-pair regrouped input: (C/8) groups x H rows x (W+1) entries x 32 bytes
-    assert lib.dcn_forward_f16_workspace_bytes(ctypes.byref(jasna)) == 16 * 64 * 65 * 32
+    # 64x64 tiles take the shared-memory slab kernel by default.
+    assert lib.dcn_forward_f16_path(ctypes.byref(jasna)) == _native.DCN_PATH_SLAB_TC
+    assert lib.dcn_packed_weight_bytes(ctypes.byref(jasna)) == 16 * 5 * 2048  # 16 groups x 5 SW32 blocks
+    # zero-bordered slabs: (C/8) groups x (H+2) x (W+2) positions x 16 bytes
+    assert lib.dcn_forward_f16_workspace_bytes(ctypes.byref(jasna)) == 16 * 66 * 66 * 16
+    # a 270x480 frame does not fit a shared-memory slab: global-gather kernel, corner pairs
+    frame = DeformConvShape.jasna_propagation(1, 270, 480).to_c()
+    assert lib.dcn_forward_f16_path(ctypes.byref(frame)) == _native.DCN_PATH_FUSED_TC
+    assert lib.dcn_packed_weight_bytes(ctypes.byref(frame)) == 18 * 8192
+    assert lib.dcn_forward_f16_workspace_bytes(ctypes.byref(frame)) == 16 * 270 * 481 * 32
     # 32 output channels -> direct path, OIHW FP16 packed weight, no workspace.
     other = DeformConvShape(1, 128, 64, 64, 32, 64, 64, 3, 3, 1, 1, 1, 1, 1, 1, 1, 16).to_c()
     assert lib.dcn_forward_f16_path(ctypes.byref(other)) == _native.DCN_PATH_DIRECT
@@ -87,6 +93,19 @@ def test_path_selection_and_sizes(lib):
     # 5x5 output plane (25 px, not a multiple of 8) -> direct path.
     odd = DeformConvShape.jasna_propagation(1, 5, 5).to_c()
     assert lib.dcn_forward_f16_path(ctypes.byref(odd)) == _native.DCN_PATH_DIRECT
+
+
+def test_kernel_choice_can_be_pinned_per_process():
+    import sys
+
+    code = ("import ctypes; from jasnamacos_b200 import _native; from jasnamacos_b200.deform_conv import "
+            "DeformConvShape as S; lib=_native.load(); s=S.jasna_propagation().to_c(); "
+            "print(lib.dcn_forward_f16_path(ctypes.byref(s)), lib.dcn_packed_weight_bytes(ctypes.byref(s)))")
+    import os
+
+    env = dict(os.environ, DCN_B200_FUSED_KERNEL="pairs", PYTHONPATH=str(REPO))
+    out = subprocess.run([sys.executable, "-c", code], env=env, capture_output=True, text=True, check=True).stdout
+    assert out.split() == [str(_native.DCN_PATH_FUSED_TC), str(18 * 8192)]
 
 
 def test_null_pointers_are_rejected_before_any_device_work(lib):

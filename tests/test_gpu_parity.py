@@ -104,7 +104,7 @@ def test_f32_config0_bit_exact(cuda_op):
 
 def test_f16_config1_fused_gates(cuda_op):
     inp = synthetic.generate(1)
-    assert cuda_op.path(inp.shape) == _native.DCN_PATH_FUSED_TC
+    assert cuda_op.path(inp.shape) == _native.DCN_PATH_SLAB_TC  # 64x64 tiles: shared-memory slab kernel
     ref = oracle.run(inp.shape, inp.input, inp.offset, inp.mask, inp.weight, inp.bias)
     out = cuda_op.run_float16(inp.shape, inp.input, inp.offset, inp.mask, inp.weight, inp.bias)
     assert out.dtype == np.float16

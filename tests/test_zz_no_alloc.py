@@ -29,7 +29,7 @@ def test_static_scratch_matches_workspace_entry_point_twice():
 
     assert torch.cuda.is_available()
     lib = _native.load()
-    shape = DeformConvShape.jasna_propagation(batch=4)  # 4 x 2.03 MiB of scratch, under 16 MiB
+    shape = DeformConvShape.jasna_propagation(batch=4)  # at most 4 x 2.03 MiB of scratch, under 16 MiB
     c_shape = shape.to_c()
     assert lib.dcn_static_scratch_bytes() == 16 << 20
     w, b = synthetic.weights(shape, 21)
@@ -61,7 +61,7 @@ def test_static_scratch_matches_workspace_entry_point_twice():
 
 def test_static_scratch_rejects_problems_beyond_its_size():
     lib = _native.load()
-    big = DeformConvShape.jasna_propagation(batch=8)  # 8 x 2.03 MiB > 16 MiB
+    big = DeformConvShape.jasna_propagation(batch=20)  # 20 tiles need more than 16 MiB on either path
     c_big = big.to_c()
     assert lib.dcn_forward_f16_workspace_bytes(ctypes.byref(c_big)) > lib.dcn_static_scratch_bytes()
     p = ctypes.c_void_p(16)  # never dereferenced: the size check comes first
