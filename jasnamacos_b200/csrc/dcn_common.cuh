@@ -113,7 +113,7 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t parity
 }
 
 
-// ---- TMA / bulk copies (no cluster multicast anywhere) --------------------------
+// ---- TMA / bulk copies (each CTA loads only for itself) -------------------------
 
 __device__ __forceinline__ void bulk_copy_g2s(void *smem_dst, const void *gmem_src, uint32_t bytes,
                                               uint64_t *bar) {
