@@ -94,19 +94,39 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
     return done != 0;
 }
 
+// try_wait that lets the hardware suspend the thread for up to `ns` nanoseconds
+// while the phase is incomplete (it resumes as soon as the phase completes).
+__device__ __forceinline__ bool mbar_try_wait_suspend(uint64_t *bar, uint32_t parity, uint32_t ns) {
+    uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(done)
+        : "r"(smem_addr(bar)), "r"(parity), "r"(ns)
+        : "memory");
+    return done != 0;
+}
+
 // Waits for the phase with the given parity to complete.  Gives up (returns
 // false) after kWaitLimitNs, or as soon as *abort becomes non-zero when `abort`
 // is given, so a broken pipeline ends the kernel with an error status instead
 // of hanging the GPU.
 // `backoff_ns` > 0 sleeps between polls (for waiters off the critical path, so
-// their polling does not take issue slots and shared-memory cycles).
+// their polling does not take issue slots and shared-memory cycles).  Critical
+// waiters poll with a hardware suspend hint instead, which wakes them as soon as
+// the phase completes.
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t parity,
                                                   volatile int *abort, uint32_t backoff_ns = 0) {
     if (mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = global_timer_ns();
     while (true) {
-        if (backoff_ns) __nanosleep(backoff_ns);
-        if (mbar_try_wait(bar, parity)) return true;
+        if (backoff_ns) {
+            __nanosleep(backoff_ns);
+            if (mbar_try_wait(bar, parity)) return true;
+        } else if (mbar_try_wait_suspend(bar, parity, 20000u)) {
+            return true;
+        }
         if (abort != nullptr && *abort) return false;
         if (global_timer_ns() - t0 > kWaitLimitNs) return false;
     }

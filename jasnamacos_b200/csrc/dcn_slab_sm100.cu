@@ -336,11 +336,34 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t lane_base = tmem + (static_cast<uint32_t>(q * 32) << 16);
         const int sw = p.W + 2;  // slab row stride in positions
         const uint32_t slab0 = smem_addr(slab_base);
+        // This warp's taps as float offsets (ky*DH, kx*DW): integer-valued, so adding
+        // them to the pixel's integer base in FP32 is exact, as in the reference.
+        float tyf[3], txf[3];
+#pragma unroll
+        for (int i = 0; i < 3; ++i) {
+            const int2 tk = s.tap[tap0 + i];
+            tyf[i] = static_cast<float>(tk.x);
+            txf[i] = static_cast<float>(tk.y);
+        }
         uint32_t gi = 0, si = 0;
         bool ok = true;
         for (int u = blockIdx.x; u < a.num_units && ok; u += gridDim.x) {
             const int t0 = (u % a.units_per_image) * a.tiles_per_unit;
             const int mt = min(a.tiles_per_unit, a.tiles_per_image - t0);
+            // Per tile of the unit: this pixel's integer sampling base (oy*SH - PH,
+            // ox*SW - PW) as floats, and whether the pixel exists (its samples are
+            // skipped, and its A row left zero, when it is past the output plane).
+            float bfy[kMaxTilesPerUnit], bfx[kMaxTilesPerUnit];
+            bool tvalid[kMaxTilesPerUnit];
+#pragma unroll
+            for (int t = 0; t < kMaxTilesPerUnit; ++t) {
+                const int px = (t0 + t) * BM + r;
+                tvalid[t] = t < mt && px < p.out_plane;
+                const int oy = tvalid[t] ? px / p.WO : 0;
+                const int ox = tvalid[t] ? px - oy * p.WO : 0;
+                bfy[t] = static_cast<float>(oy * p.SH - p.PH);
+                bfx[t] = static_cast<float>(ox * p.SW - p.PW);
+            }
             for (int g = 0; g < OG && ok; ++g, ++gi) {
                 const uint32_t gb = gi & 1u, gph = (gi >> 1) & 1u;
                 if (!mbar_wait_bounded(&s.grp_full[gb], gph, abort_flag)) {
@@ -348,12 +371,12 @@ __global__ void __launch_bounds__(kThreads, 1)
                     break;
                 }
                 const uint32_t slab = slab0 + gb * slab_stride;
-                for (int t = 0; t < mt; ++t, ++si) {
+#pragma unroll
+                for (int t = 0; t < kMaxTilesPerUnit; ++t) {
+                    if (t >= mt) break;
                     const uint32_t st = si % kStages, ph = (si / kStages) & 1u;
-                    const int px = (t0 + t) * BM + r;
-                    const bool valid = px < p.out_plane;
-                    const int oy = valid ? px / p.WO : 0;
-                    const int ox = valid ? px - oy * p.WO : 0;
+                    ++si;
+                    const bool valid = tvalid[t];
                     if (!mbar_wait_bounded(&s.om_full[st], ph, abort_flag)) {
                         ok = false;
                         break;
@@ -364,9 +387,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
                     for (int i = 0; i < 3; ++i) {
                         const int k = tap0 + i;
-                        const int2 tk = s.tap[k];
-                        const float y = static_cast<float>(oy * p.SH - p.PH + tk.x) + __half2float(s.off[st][2 * k][r]);
-                        const float x = static_cast<float>(ox * p.SW - p.PW + tk.y) + __half2float(s.off[st][2 * k + 1][r]);
+                        const float y = (bfy[t] + tyf[i]) + __half2float(s.off[st][2 * k][r]);
+                        const float x = (bfx[t] + txf[i]) + __half2float(s.off[st][2 * k + 1][r]);
                         m[i] = __half2float(s.msk[st][k][r]);
                         const int y0 = __float2int_rd(y);
                         const int x0 = __float2int_rd(x);
