@@ -210,6 +210,23 @@ dcn_status dcn_forward_f16_grouped(const dcn_shape *shape, const void *input_gro
                                    const void *bias, void *output, uint32_t *nonfinite_flag,
                                    dcn_stream stream);
 
+/* ---- offset producer fused into the convolution ------------------------------------
+ * prepare_dcn_offsets_fp16 (MetalShader.swift:817-839) followed by the DCN, as the
+ * production graph chains them (FusedFourPassRecurrenceProbe.swift:609-630), in one
+ * operator: `raw` is the offset network's output [N][3*G*KH*KW][Ho][Wo] FP16 (2*G*KH*KW
+ * offset residues, then G*KH*KW mask logits; 432 channels for Jasna), flow1/flow2 are
+ * [N][2][Ho][Wo] FP16 in (x, y) order.  offset = FP16(10*tanh(residue) + flow) with dy
+ * channels taking the flow's y row and deformable groups [0, G/2) flow1, the rest flow2;
+ * mask = FP16(sigmoid(logit)).  On the slab path the transform runs inside the
+ * convolution and the offset/mask tensors never exist in memory; other tensor-core
+ * shapes run the offset producer into the workspace first.  Requires an even G and a
+ * tensor-core path (else DCN_ERR_UNSUPPORTED); raw and flows 16-byte aligned. */
+size_t dcn_forward_f16_raw_workspace_bytes(const dcn_shape *shape);
+dcn_status dcn_forward_f16_raw(const dcn_shape *shape, const void *input, const void *raw,
+                               const void *flow1, const void *flow2, const void *packed_weight,
+                               const void *bias, void *output, uint32_t *nonfinite_flag,
+                               void *workspace, size_t workspace_bytes, dcn_stream stream);
+
 /* ---- non-finite detection -----------------------------------------------------
  * flag_non_finite_fp16 (MetalShader.swift:454-463): ORs DCN_FLAG_NONFINITE into
  * *flag if any of `count` FP16 values is Inf or NaN. */

@@ -26,8 +26,12 @@ cudaError_t launch_prepack_weights(const Params &p, bool fused, int kb, const vo
                                    int layout, void *dst, cudaStream_t stream);
 cudaError_t launch_flag_non_finite(const __half *values, int64_t count, uint32_t *flag, int sm_count,
                                    cudaStream_t stream);
-cudaError_t launch_prepare_offsets(int64_t plane, const __half *raw, const __half *flow1, const __half *flow2,
-                                   __half *offset, __half *mask, cudaStream_t stream);
+cudaError_t launch_prepare_offsets(int64_t n_images, int gka, int64_t plane, const __half *raw, const __half *flow1,
+                                   const __half *flow2, __half *offset, __half *mask, cudaStream_t stream);
+cudaError_t launch_slab_grouped_raw(const Params &p, const void *slabs, const __half *raw, const __half *flow1,
+                                    const __half *flow2, const uint8_t *packed_w, const __half *bias,
+                                    __half *output, uint32_t *flag, int sm_count, uint32_t *err,
+                                    cudaStream_t stream);
 bool fused_supported(const Params &p);
 int fused_kblocks(const Params &p);
 size_t fused_workspace_bytes(const Params &p);
@@ -404,10 +408,67 @@ dcn_status dcn_prepare_offsets_f16(int64_t plane, const void *raw, const void *f
     DeviceInfo *dev = nullptr;
     dcn_status st = current_device(&dev);
     if (st != DCN_OK) return st;
-    return from_cuda(launch_prepare_offsets(plane, static_cast<const __half *>(raw),
+    return from_cuda(launch_prepare_offsets(1, 144, plane, static_cast<const __half *>(raw),
                                             static_cast<const __half *>(flow1), static_cast<const __half *>(flow2),
                                             static_cast<__half *>(offset), static_cast<__half *>(mask),
                                             reinterpret_cast<cudaStream_t>(stream)));
+}
+
+namespace {
+
+size_t round256(size_t v) { return (v + 255) & ~size_t{255}; }
+
+// Bytes of the FP16 offset and mask tensors of a shape (the two-step form of the raw entry point).
+size_t offset_bytes(const Params &p) { return round256(static_cast<size_t>(p.N) * 2 * p.OG * p.KA * p.out_plane * 2); }
+size_t mask_bytes(const Params &p) { return round256(static_cast<size_t>(p.N) * p.OG * p.KA * p.out_plane * 2); }
+
+}  // namespace
+
+size_t dcn_forward_f16_raw_workspace_bytes(const dcn_shape *shape) {
+    if (validate(shape) != DCN_OK) return 0;
+    const Params p = make_params(*shape);
+    const dcn_path path = select_path(p);
+    if (path == DCN_PATH_DIRECT || p.OG % 2 != 0) return 0;
+    const size_t base = round256(dcn_forward_f16_workspace_bytes(shape));
+    return path == DCN_PATH_SLAB_TC ? base : base + offset_bytes(p) + mask_bytes(p);
+}
+
+dcn_status dcn_forward_f16_raw(const dcn_shape *shape, const void *input, const void *raw, const void *flow1,
+                               const void *flow2, const void *packed_weight, const void *bias, void *output,
+                               uint32_t *nonfinite_flag, void *workspace, size_t workspace_bytes,
+                               dcn_stream stream) {
+    dcn_status st = validate(shape);
+    if (st != DCN_OK) return st;
+    const Params p = make_params(*shape);
+    const dcn_path path = select_path(p);
+    if (path == DCN_PATH_DIRECT || p.OG % 2 != 0) return DCN_ERR_UNSUPPORTED;
+    if (!input || !raw || !flow1 || !flow2 || !packed_weight || !bias || !output) return DCN_ERR_INVALID_ARGUMENT;
+    if (!aligned(input, 2) || !aligned(raw, 16) || !aligned(flow1, 16) || !aligned(flow2, 16) ||
+        !aligned(packed_weight, 16) || !aligned(bias, 2) || !aligned(output, 2) ||
+        (nonfinite_flag && !aligned(nonfinite_flag, 4)))
+        return DCN_ERR_INVALID_ARGUMENT;
+    if (!workspace || !aligned(workspace, 256) || workspace_bytes < dcn_forward_f16_raw_workspace_bytes(shape))
+        return DCN_ERR_INVALID_ARGUMENT;
+    DeviceInfo *dev = nullptr;
+    if ((st = current_device(&dev)) != DCN_OK) return st;
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    const auto *r = static_cast<const __half *>(raw);
+    const auto *f1 = static_cast<const __half *>(flow1);
+    const auto *f2 = static_cast<const __half *>(flow2);
+    cudaError_t e = launch_regroup(path, p, input, workspace, s);
+    if (e != cudaSuccess) return from_cuda(e);
+    if (path == DCN_PATH_SLAB_TC)
+        return from_cuda(launch_slab_grouped_raw(p, workspace, r, f1, f2, static_cast<const uint8_t *>(packed_weight),
+                                                 static_cast<const __half *>(bias), static_cast<__half *>(output),
+                                                 nonfinite_flag, dev->sm_count, dev->err_word, s));
+    // Two steps for the global-gather kernel: the offset producer into the workspace, then the operator.
+    uint8_t *ws = static_cast<uint8_t *>(workspace);
+    const size_t base = round256(dcn_forward_f16_workspace_bytes(shape));
+    auto *offset = reinterpret_cast<__half *>(ws + base);
+    auto *mask = reinterpret_cast<__half *>(ws + base + offset_bytes(p));
+    e = launch_prepare_offsets(p.N, p.OG * p.KA, p.out_plane, r, f1, f2, offset, mask, s);
+    if (e != cudaSuccess) return from_cuda(e);
+    return launch_grouped(path, p, workspace, offset, mask, packed_weight, bias, output, nonfinite_flag, dev, s);
 }
 
 dcn_status dcn_device_error(void) {

@@ -25,24 +25,29 @@ __global__ void flag_non_finite_kernel(const __half *__restrict__ values, int64_
     if (__any_sync(0xffffffffu, bad) && (threadIdx.x % 32) == 0) atomicOr(flag, DCN_FLAG_NONFINITE);
 }
 
-// One thread per (channel, spatial) of the 432-channel raw tensor.
-__global__ void prepare_offsets_kernel(int64_t plane, const __half *__restrict__ raw,
+// One thread per (image, channel, spatial) of the raw tensor [N][3*gka][plane]
+// (gka = deformable groups x taps; 144 for Jasna: 288 offset residues + 144 mask logits).
+// Offset channels [0, gka) take flow1, [gka, 2*gka) flow2.
+__global__ void prepare_offsets_kernel(int64_t n_images, int gka, int64_t plane, const __half *__restrict__ raw,
                                        const __half *__restrict__ flow1, const __half *__restrict__ flow2,
                                        __half *__restrict__ offset, __half *__restrict__ mask) {
     const int64_t gid = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-    if (gid >= 432 * plane) return;
-    const int64_t channel = gid / plane;
-    const int64_t spatial = gid % plane;
+    const int64_t per_image = 3 * static_cast<int64_t>(gka) * plane;
+    if (gid >= n_images * per_image) return;
+    const int64_t n = gid / per_image;
+    const int64_t rest = gid % per_image;
+    const int64_t channel = rest / plane;
+    const int64_t spatial = rest % plane;
     const float v = __half2float(raw[gid]);
-    if (channel < 288) {
-        const int64_t local = channel % 144;
-        const __half *flow = channel < 144 ? flow1 : flow2;
+    if (channel < 2 * gka) {
+        const int64_t local = channel % gka;
+        const __half *flow = (channel < gka ? flow1 : flow2) + n * 2 * plane;
         // The flow is stored (x, y); offsets are interleaved (dy, dx), so even channels take row 1.
         const int64_t flow_channel = (local & 1) == 0 ? 1 : 0;
         const float residue = 10.0f * tanhf(v);
-        offset[gid] = __float2half_rn(residue + __half2float(flow[flow_channel * plane + spatial]));
+        offset[n * 2 * gka * plane + rest] = __float2half_rn(residue + __half2float(flow[flow_channel * plane + spatial]));
     } else {
-        mask[(channel - 288) * plane + spatial] = __float2half_rn(1.0f / (1.0f + expf(-v)));
+        mask[(n * gka + channel - 2 * gka) * plane + spatial] = __float2half_rn(1.0f / (1.0f + expf(-v)));
     }
 }
 
@@ -58,11 +63,11 @@ cudaError_t launch_flag_non_finite(const __half *values, int64_t count, uint32_t
     return cudaGetLastError();
 }
 
-cudaError_t launch_prepare_offsets(int64_t plane, const __half *raw, const __half *flow1, const __half *flow2,
-                                   __half *offset, __half *mask, cudaStream_t stream) {
-    const int64_t total = 432 * plane;
+cudaError_t launch_prepare_offsets(int64_t n_images, int gka, int64_t plane, const __half *raw, const __half *flow1,
+                                   const __half *flow2, __half *offset, __half *mask, cudaStream_t stream) {
+    const int64_t total = n_images * 3 * gka * plane;
     prepare_offsets_kernel<<<static_cast<unsigned>((total + 255) / 256), 256, 0, stream>>>(
-        plane, raw, flow1, flow2, offset, mask);
+        n_images, gka, plane, raw, flow1, flow2, offset, mask);
     return cudaGetLastError();
 }
 

@@ -48,6 +48,7 @@ constexpr int kStages = 4;                                // (tile, group) stage
 constexpr int kOffRows = 2 * kTaps;                       // 18 offset rows per (tile, group)
 constexpr int kMaskRows = kTaps;                          // 9 mask rows
 constexpr uint32_t kStageTxBytes = (kOffRows + kMaskRows) * BM * 2;
+constexpr uint32_t kFlowTxBytes = 2 * BM * 2;
 constexpr int kProducerWarps = 12;  // 3 per TMEM lane quarter, 3 taps each
 constexpr int kEpilogueWarps = 4;
 constexpr int kThreads = (4 + kEpilogueWarps + kProducerWarps) * 32;  // 640
@@ -55,13 +56,14 @@ constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kACol0 = kMaxTilesPerUnit * BN;  // 256: A stages after the accumulators
 constexpr uint32_t kAStageCols = kChunks * 4;       // 40 columns per stage
 constexpr uint32_t kIdleBackoffNs = 200;
-constexpr int kMaxSlabBytes = 88 * 1024;            // two slabs + ~49 KB of fixed buffers fit 227 KB
+constexpr int kMaxSlabBytes = 87 * 1024;            // two slabs + ~51 KB of fixed buffers fit 227 KB
 
 // Shared memory: fixed part; the two slabs follow it (size depends on H, W).
 struct __align__(1024) Smem {
     uint8_t b[2][kBGroupBytes];           // weight slices of the two buffered groups (256-aligned)
-    __half off[kStages][kOffRows][BM];    // TMA boxes
-    __half msk[kStages][kMaskRows][BM];
+    __half off[kStages][kOffRows][BM];    // TMA boxes: offsets (or raw offset residues)
+    __half msk[kStages][kMaskRows][BM];   // masks (or raw mask logits)
+    __half flow[kStages][2][BM];          // (x, y) flow rows of the stage (raw-input form only)
     float bias[BN];
     int2 tap[kTaps];                      // {ky*DH, kx*DW}
     uint64_t grp_full[2];                 // slab + weights of a group landed
@@ -84,6 +86,7 @@ struct Args {
     __half *out;
     uint32_t *flag;
     uint32_t *err;
+    int raw_mask_channel0;     // raw form: first mask-logit channel (2 * OG * KA)
     int slab_bytes;            // (H+2)(W+2)*16
     int tiles_per_image;
     int tiles_per_unit;        // 1..4
@@ -96,6 +99,13 @@ __device__ __forceinline__ uint32_t pack_half2(__half2 h) { return *reinterpret_
 __device__ __forceinline__ void signal_abort(Smem &s, uint32_t *err) {
     s.abort_flag = 1;
     atomicOr(err, kErrWaitTimeout);
+}
+
+// Hardware tanh approximation (sm_75+ tanh.approx.f32, ~2^-11 relative error).
+__device__ __forceinline__ float tanh_approx(float x) {
+    float y;
+    asm("tanh.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
 }
 
 __device__ __forceinline__ uint4 lds128(uint32_t addr) {
@@ -116,8 +126,16 @@ __device__ __forceinline__ uint64_t make_sw32_kmajor_desc(uint32_t smem_byte_add
     return d;
 }
 
+// FromRaw = false: offsets and masks are inputs (the reference's DCN call).
+// FromRaw = true: the inputs are the offset network's raw output and the two flows,
+// transformed here as prepare_dcn_offsets_fp16 does (MetalShader.swift:817-839):
+// offset = half(10*tanh(residue) + flow), mask = half(sigmoid(logit)); the flow is
+// stored (x, y), dy channels take its y row, and deformable groups [0, OG/2) use
+// flow1, the rest flow2.  tmap_flow1/2 are unused when FromRaw is false.
+template <bool FromRaw>
 __global__ void __launch_bounds__(kThreads, 1)
     slab_dcn_kernel(const __grid_constant__ CUtensorMap tmap_off, const __grid_constant__ CUtensorMap tmap_msk,
+                    const __grid_constant__ CUtensorMap tmap_flow1, const __grid_constant__ CUtensorMap tmap_flow2,
                     const Args a) {
     extern __shared__ uint8_t smem_raw[];
     Smem &s = *reinterpret_cast<Smem *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t{1023});
@@ -158,6 +176,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (warp == 0 && lane == 0) {
         prefetch_tensor_map(&tmap_off);
         prefetch_tensor_map(&tmap_msk);
+        if (FromRaw) {
+            prefetch_tensor_map(&tmap_flow1);
+            prefetch_tensor_map(&tmap_flow2);
+        }
     }
     tc_fence_before();
     __syncthreads();
@@ -209,10 +231,14 @@ __global__ void __launch_bounds__(kThreads, 1)
                             ok = false;
                             break;
                         }
-                        mbar_arrive_expect_tx(&s.om_full[st], kStageTxBytes);
+                        mbar_arrive_expect_tx(&s.om_full[st], kStageTxBytes + (FromRaw ? kFlowTxBytes : 0u));
                         const int px0 = (t0 + t) * BM;
                         tma_load_3d(&s.off[st][0][0], &tmap_off, &s.om_full[st], px0, kOffRows * g, n);
-                        tma_load_3d(&s.msk[st][0][0], &tmap_msk, &s.om_full[st], px0, kMaskRows * g, n);
+                        tma_load_3d(&s.msk[st][0][0], &tmap_msk, &s.om_full[st], px0,
+                                    (FromRaw ? a.raw_mask_channel0 : 0) + kMaskRows * g, n);
+                        if (FromRaw)
+                            tma_load_3d(&s.flow[st][0][0], g < OG / 2 ? &tmap_flow1 : &tmap_flow2, &s.om_full[st],
+                                        px0, 0, n);
                     }
                 }
             }
@@ -387,9 +413,20 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
                     for (int i = 0; i < 3; ++i) {
                         const int k = tap0 + i;
-                        const float y = (bfy[t] + tyf[i]) + __half2float(s.off[st][2 * k][r]);
-                        const float x = (bfx[t] + txf[i]) + __half2float(s.off[st][2 * k + 1][r]);
-                        m[i] = __half2float(s.msk[st][k][r]);
+                        float off_y = __half2float(s.off[st][2 * k][r]);
+                        float off_x = __half2float(s.off[st][2 * k + 1][r]);
+                        float mk = __half2float(s.msk[st][k][r]);
+                        if (FromRaw) {
+                            // Rounded to FP16 like the reference's intermediate tensors.
+                            off_y = __half2float(__float2half_rn(10.0f * tanh_approx(off_y) +
+                                                                 __half2float(s.flow[st][1][r])));
+                            off_x = __half2float(__float2half_rn(10.0f * tanh_approx(off_x) +
+                                                                 __half2float(s.flow[st][0][r])));
+                            mk = __half2float(__float2half_rn(__frcp_rn(1.0f + __expf(-mk))));
+                        }
+                        const float y = (bfy[t] + tyf[i]) + off_y;
+                        const float x = (bfx[t] + txf[i]) + off_x;
+                        m[i] = mk;
                         const int y0 = __float2int_rd(y);
                         const int x0 = __float2int_rd(x);
                         fy[i] = y - static_cast<float>(y0);
@@ -546,7 +583,10 @@ cudaError_t slab_prepare_device() {
     // Opt in to the largest dynamic shared memory any supported shape needs.
     const int max_slab = (slab::kMaxSlabBytes + 127) & ~127;
     const size_t smem = 1024 + ((sizeof(slab::Smem) + 127) & ~size_t{127}) + 2 * static_cast<size_t>(max_slab);
-    return cudaFuncSetAttribute(slab::slab_dcn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    cudaError_t e = cudaFuncSetAttribute(slab::slab_dcn_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(smem));
+    if (e != cudaSuccess) return e;
+    return cudaFuncSetAttribute(slab::slab_dcn_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                 static_cast<int>(smem));
 }
 
@@ -576,14 +616,11 @@ namespace fused {
 bool make_plane_map(CUtensorMap *map, const void *base, int64_t plane, int channels, int batch, int rows);
 }
 
-cudaError_t launch_slab_grouped(const Params &p, const void *slabs, const __half *offset, const __half *mask,
-                                const uint8_t *packed_w, const __half *bias, __half *output, uint32_t *flag,
-                                int sm_count, uint32_t *err, cudaStream_t stream) {
+namespace {
+
+slab::Args make_slab_args(const Params &p, const void *slabs, const uint8_t *packed_w, const __half *bias,
+                          __half *output, uint32_t *flag, int sm_count, uint32_t *err) {
     using namespace slab;
-    CUtensorMap tmap_off, tmap_msk;
-    if (!fused::make_plane_map(&tmap_off, offset, p.out_plane, 2 * p.OG * p.KA, p.N, kOffRows) ||
-        !fused::make_plane_map(&tmap_msk, mask, p.out_plane, p.OG * p.KA, p.N, kMaskRows))
-        return cudaErrorInvalidValue;
     Args a;
     a.p = p;
     a.slabs = static_cast<const uint8_t *>(slabs);
@@ -592,6 +629,7 @@ cudaError_t launch_slab_grouped(const Params &p, const void *slabs, const __half
     a.out = output;
     a.flag = flag;
     a.err = err;
+    a.raw_mask_channel0 = 2 * p.OG * p.KA;
     a.slab_bytes = (p.H + 2) * (p.W + 2) * 16;
     a.tiles_per_image = (p.out_plane + BM - 1) / BM;
     // Up to 4 tiles per work unit (each unit reads every group's slab once); fewer
@@ -601,8 +639,41 @@ cudaError_t launch_slab_grouped(const Params &p, const void *slabs, const __half
     a.tiles_per_unit = tpu;
     a.units_per_image = (a.tiles_per_image + tpu - 1) / tpu;
     a.num_units = p.N * a.units_per_image;
+    return a;
+}
+
+}  // namespace
+
+cudaError_t launch_slab_grouped(const Params &p, const void *slabs, const __half *offset, const __half *mask,
+                                const uint8_t *packed_w, const __half *bias, __half *output, uint32_t *flag,
+                                int sm_count, uint32_t *err, cudaStream_t stream) {
+    using namespace slab;
+    CUtensorMap tmap_off, tmap_msk;
+    if (!fused::make_plane_map(&tmap_off, offset, p.out_plane, 2 * p.OG * p.KA, p.N, kOffRows) ||
+        !fused::make_plane_map(&tmap_msk, mask, p.out_plane, p.OG * p.KA, p.N, kMaskRows))
+        return cudaErrorInvalidValue;
+    const Args a = make_slab_args(p, slabs, packed_w, bias, output, flag, sm_count, err);
     const int grid = a.num_units < sm_count ? a.num_units : sm_count;
-    slab_dcn_kernel<<<grid, kThreads, slab_smem_bytes(p), stream>>>(tmap_off, tmap_msk, a);
+    slab_dcn_kernel<false><<<grid, kThreads, slab_smem_bytes(p), stream>>>(tmap_off, tmap_msk, tmap_off, tmap_msk, a);
+    return cudaGetLastError();
+}
+
+// raw: [N][3*OG*KA][plane] (offset residues, then mask logits); flow1/flow2: [N][2][plane].
+cudaError_t launch_slab_grouped_raw(const Params &p, const void *slabs, const __half *raw, const __half *flow1,
+                                    const __half *flow2, const uint8_t *packed_w, const __half *bias,
+                                    __half *output, uint32_t *flag, int sm_count, uint32_t *err,
+                                    cudaStream_t stream) {
+    using namespace slab;
+    CUtensorMap tmap_off, tmap_msk, tmap_f1, tmap_f2;
+    const int raw_channels = 3 * p.OG * p.KA;
+    if (!fused::make_plane_map(&tmap_off, raw, p.out_plane, raw_channels, p.N, kOffRows) ||
+        !fused::make_plane_map(&tmap_msk, raw, p.out_plane, raw_channels, p.N, kMaskRows) ||
+        !fused::make_plane_map(&tmap_f1, flow1, p.out_plane, 2, p.N, 2) ||
+        !fused::make_plane_map(&tmap_f2, flow2, p.out_plane, 2, p.N, 2))
+        return cudaErrorInvalidValue;
+    const Args a = make_slab_args(p, slabs, packed_w, bias, output, flag, sm_count, err);
+    const int grid = a.num_units < sm_count ? a.num_units : sm_count;
+    slab_dcn_kernel<true><<<grid, kThreads, slab_smem_bytes(p), stream>>>(tmap_off, tmap_msk, tmap_f1, tmap_f2, a);
     return cudaGetLastError();
 }
 

@@ -368,6 +368,35 @@ class CudaDeformConv:
         raise_for_status(st, "dcn_forward_f16_grouped")
         return out
 
+    def forward_f16_raw(self, shape, input, raw, flow1, flow2, packed_weight, bias, out=None, flag=None,
+                        workspace=None, stream=None):
+        """Offset producer + DCNv2 in one operator: `raw` is the offset network's output
+        [N][3*G*9][Ho][Wo] (residues, then mask logits), flows [N][2][Ho][Wo] in (x, y) order;
+        replaces prepare_dcn_offsets_fp16 (MetalShader.swift:817-839) followed by the convolution."""
+        torch = _torch()
+        gka = shape.offset_groups * shape.kernel_area
+        plane = shape.output_height * shape.output_width
+        for name, arr, want in (("input", input, shape.input_count), ("raw", raw, shape.batch * 3 * gka * plane),
+                                ("flow1", flow1, shape.batch * 2 * plane), ("flow2", flow2, shape.batch * 2 * plane),
+                                ("bias", bias, shape.output_channels)):
+            if arr.numel() != want:
+                raise InvalidArrayCount(name, want, arr.numel())
+        if out is None:
+            out = torch.empty(shape.output_count, dtype=torch.float16, device=input.device)
+        ws_bytes = int(self.lib.dcn_forward_f16_raw_workspace_bytes(ctypes.byref(shape.to_c())))
+        if ws_bytes == 0:
+            raise Unsupported("shape does not take a tensor-core path with an even deformable-group count")
+        if workspace is None:
+            workspace = torch.empty(ws_bytes, dtype=torch.uint8, device=input.device)
+        self._check_device(input, raw, flow1, flow2, packed_weight, bias, out, flag, workspace)
+        with torch.cuda.device(input.device):
+            st = self.lib.dcn_forward_f16_raw(
+                ctypes.byref(shape.to_c()), _ptr(input), _ptr(raw), _ptr(flow1), _ptr(flow2), _ptr(packed_weight),
+                _ptr(bias), _ptr(out), _ptr(flag), _ptr(workspace), workspace.numel() * workspace.element_size(),
+                _stream_handle(stream))
+        raise_for_status(st, "dcn_forward_f16_raw")
+        return out
+
     def flag_non_finite(self, values, flag, stream=None):
         """flag_non_finite_fp16 (MetalShader.swift:454-463)."""
         self._check_device(values, flag)
