@@ -251,34 +251,71 @@ def event_time_ms(fn, iters: int, stream=None) -> float:
     return a.elapsed_time(b)
 
 
+# Benchmark configurations.  Tile batches (2, 4) are sharded over the GPUs (total work
+# fixed: "strong"); single-image configurations (0, 1, 3) run one replica per GPU ("weak").
+CONFIGS = {
+    0: dict(desc="config 0: FP32 1x128x64x64 -> 1x64x64x64, 3x3, pad 1, 16 deformable groups, offsets N(0,2^2), "
+                 "mask sigmoid(N(0,1))", images=1, flow=None, f32=True, sharded=False),
+    1: dict(desc="config 1: FP16 1x128x64x64 -> 1x64x64x64, 3x3, pad 1, 16 deformable groups, offsets N(0,2^2), "
+                 "mask sigmoid(N(0,1)), weights prepacked once", images=1, flow=None, f32=False, sharded=False),
+    2: dict(desc="config 2: N=128 FP16 tiles of 128x64x64 -> 64x64x64, 3x3, pad 1, 16 deformable groups, "
+                 "offsets 10*tanh(N(0,1)) + flow U(-16,16)", images=128, flow=16.0, f32=False, sharded=True),
+    3: dict(desc="config 3: FP16 1x128x270x480 -> 1x64x270x480, 3x3, pad 1, 16 deformable groups, "
+                 "offsets 10*tanh(N(0,1)) + flow U(-32,32)", images=1, flow=32.0, f32=False, sharded=False),
+    4: dict(desc="config 4: N=2048 FP16 tiles of 128x64x64 -> 64x64x64, 3x3, pad 1, 16 deformable groups, "
+                 "offsets 10*tanh(N(0,1)) + flow U(-16,16), sharded evenly over the GPUs", images=TILES, flow=16.0,
+            f32=False, sharded=True),
+}
+
+
 def run_ours(args):
-    import numpy as np
     import torch
 
-    from jasnamacos_b200 import synthetic
+    from jasnamacos_b200 import _native, synthetic
     from jasnamacos_b200.deform_conv import CudaDeformConv
 
     rank, world, local, pg = dist_setup(args.gpus)
     dev = torch.device("cuda", local)
     op = CudaDeformConv(local)
     peaks, peak_kind = load_peaks()
+    cfg = CONFIGS[args.config]
 
-    tiles = args.tiles
-    t_begin = tiles * rank // world
-    t_end = tiles * (rank + 1) // world
-    shape = synthetic.config_shape(4, batch=t_end - t_begin)
+    total_images = args.tiles if args.config == 4 else cfg["images"]
+    if cfg["sharded"]:
+        i_begin, i_end = total_images * rank // world, total_images * (rank + 1) // world
+        job_images = total_images
+    else:
+        i_begin, i_end = 0, total_images
+        job_images = total_images * world
+    base_shape = synthetic.config_shape(args.config, batch=1)
+    shape = base_shape.with_batch(i_end - i_begin)
     px_per_step = shape.output_pixels
-    x, off, msk, w, b = synthetic.device_batch(shape, 16.0, seed=1000 + t_begin, device=dev)
-    w16 = torch.from_numpy(w).to(dev).half()
-    b16 = torch.from_numpy(b).to(dev).half()
-    packed = op.prepack(shape, w16)
-    out = torch.empty(shape.output_count, dtype=torch.float16, device=dev)
+    job_px = job_images * base_shape.output_pixels
+    if cfg["f32"]:
+        x, off, msk, w, b = synthetic.device_gaussian_batch(shape, seed=1000 + i_begin, device=dev,
+                                                            dtype=torch.float32)
+    elif cfg["flow"] is None:
+        x, off, msk, w, b = synthetic.device_gaussian_batch(shape, seed=1000 + i_begin, device=dev)
+    else:
+        x, off, msk, w, b = synthetic.device_batch(shape, cfg["flow"], seed=1000 + i_begin, device=dev)
+    path = _native.DCN_PATH_DIRECT if cfg["f32"] else op.path(shape)
+    out = torch.empty(shape.output_count, dtype=torch.float32 if cfg["f32"] else torch.float16, device=dev)
     flag = torch.zeros(1, dtype=torch.int32, device=dev)
-    ws = torch.empty(op.workspace_bytes(shape), dtype=torch.uint8, device=dev)
-    torch.cuda.synchronize(dev)
+    if cfg["f32"]:
+        w32 = torch.from_numpy(w).to(dev)
+        b32 = torch.from_numpy(b).to(dev)
 
-    def step():
-        op.forward_f16(shape, x, off, msk, packed, b16, out=out, flag=flag, workspace=ws)
+        def step():
+            op.forward_f32(shape, x, off, msk, w32, b32, out=out)
+    else:
+        w16 = torch.from_numpy(w).to(dev).half()
+        b16 = torch.from_numpy(b).to(dev).half()
+        packed = op.prepack(shape, w16)
+        ws = torch.empty(max(op.workspace_bytes(shape), 16), dtype=torch.uint8, device=dev)
+
+        def step():
+            op.forward_f16(shape, x, off, msk, packed, b16, out=out, flag=flag, workspace=ws)
+    torch.cuda.synchronize(dev)
 
     # ---- device-resident throughput (the `value`) --------------------------------
     for _ in range(max(args.warmup, 3)):
@@ -295,47 +332,74 @@ def run_ours(args):
     clocks = sampler.stop()
     ms_max = max_over_ranks(ms, pg)
     ms_per_step = ms_max / args.steps
-    value = tiles * TILE_H * TILE_W / (ms_per_step * 1e-3) / 1e6  # whole job, Mpx/s
+    value = job_px / (ms_per_step * 1e-3) / 1e6  # whole job, Mpx/s
     op.device_error()
     nonfinite = int(flag.item())
 
     # ---- dominant kernel alone, for the roofline ----------------------------------
-    op.regroup_input(shape, x, workspace=ws)
-    fused_ms = event_time_ms(
-        lambda: op.forward_f16_grouped(shape, ws, off, msk, packed, b16, out=out, flag=flag), args.steps) / args.steps
-    regroup_ms = event_time_ms(lambda: op.regroup_input(shape, x, workspace=ws), args.steps) / args.steps
+    tensor_path = path in (_native.DCN_PATH_SLAB_TC, _native.DCN_PATH_FUSED_TC)
+    kernel = {_native.DCN_PATH_SLAB_TC: "slab_dcn_kernel", _native.DCN_PATH_FUSED_TC: "fused_dcn_kernel"}.get(
+        path, "direct_kernel")
+    regroup_ms = None
+    if tensor_path:
+        op.regroup_input(shape, x, workspace=ws)
+        kernel_ms = event_time_ms(lambda: op.forward_f16_grouped(shape, ws, off, msk, packed, b16, out=out, flag=flag),
+                                  args.steps) / args.steps
+        regroup_ms = event_time_ms(lambda: op.regroup_input(shape, x, workspace=ws), args.steps) / args.steps
+        launches_per_step = 2
+    else:
+        kernel_ms = ms / args.steps
+        launches_per_step = 1 if cfg["f32"] else 2
     torch.cuda.synchronize(dev)
-    achieved_gbs = BYTES_PER_PX * px_per_step / (fused_ms * 1e-3) / 1e9
-    tensor_tflops = FLOPS_PER_PX * px_per_step / (fused_ms * 1e-3) / 1e12
-    from jasnamacos_b200 import _native
-
-    kernel = {_native.DCN_PATH_SLAB_TC: "slab_dcn_kernel",
-              _native.DCN_PATH_FUSED_TC: "fused_dcn_kernel"}.get(op.path(shape), "direct_kernel")
+    bytes_per_px = BYTES_PER_PX * (2 if cfg["f32"] else 1)
+    achieved_gbs = bytes_per_px * px_per_step / (kernel_ms * 1e-3) / 1e9
+    tensor_tflops = FLOPS_PER_PX * px_per_step / (kernel_ms * 1e-3) / 1e12
     traffic = None
     prof = REPO / "profiles" / f"{kernel}_traffic.json"
-    if prof.exists():
+    if prof.exists() and args.config in (2, 4):  # captured on config-4 tiles
         d = json.loads(prof.read_text())
         traffic = d.get("dram_bytes_per_output_px", 0) * px_per_step or None
+
+    # ---- offset producer fused in (FP16 tensor-core configs with even groups) -----------
+    raw_form = None
+    if tensor_path and not args.no_raw and op.raw_workspace_bytes(shape) > 0:
+        raw, f1, f2 = synthetic.device_raw_batch(shape, cfg["flow"] or 16.0, seed=2000 + i_begin, device=dev)
+        wsr = torch.empty(op.raw_workspace_bytes(shape), dtype=torch.uint8, device=dev)
+        raw_step = lambda: op.forward_f16_raw(shape, x, raw, f1, f2, packed, b16, out=out, flag=flag,  # noqa: E731
+                                              workspace=wsr)
+        for _ in range(3):
+            raw_step()
+        barrier(pg)
+        r_ms = max_over_ranks(event_time_ms(raw_step, args.steps), pg) / args.steps
+        raw_form = {"value": job_px / (r_ms * 1e-3) / 1e6, "unit": "Mpx/s", "ms_per_step": r_ms,
+                    "what": "dcn_forward_f16_raw: offset network output (3*G*9 ch) + two flows in, offsets/masks "
+                            "computed inside the kernel (prepare_dcn_offsets_fp16 fused)"}
+        del raw, f1, f2, wsr
 
     # ---- end to end through the host-buffer API ------------------------------------
     e2e = None
     if not args.no_e2e:
-        one = shape.with_batch(1)
-        h_x = torch.empty(shape.input_count, dtype=torch.float16, pin_memory=True)
-        h_off = torch.empty(shape.offset_count, dtype=torch.float16, pin_memory=True)
-        h_msk = torch.empty(shape.mask_count, dtype=torch.float16, pin_memory=True)
-        h_out = torch.empty(shape.output_count, dtype=torch.float16, pin_memory=True)
-        h_x.copy_(x)
-        h_off.copy_(off)
-        h_msk.copy_(msk)
-        e2e_step = lambda: op.forward_f16_host(shape, h_x, h_off, h_msk, packed, b16, h_out,  # noqa: E731
-                                               chunk_images=64)
+        pin = lambda t: torch.empty(t.numel(), dtype=t.dtype, pin_memory=True).copy_(t)  # noqa: E731
+        h_x, h_off, h_msk = pin(x), pin(off), pin(msk)
+        h_out = torch.empty(out.numel(), dtype=out.dtype, pin_memory=True)
+        if cfg["f32"]:
+            d_x, d_off, d_msk = torch.empty_like(x), torch.empty_like(off), torch.empty_like(msk)
+
+            def e2e_step():
+                d_x.copy_(h_x, non_blocking=True)
+                d_off.copy_(h_off, non_blocking=True)
+                d_msk.copy_(h_msk, non_blocking=True)
+                op.forward_f32(shape, d_x, d_off, d_msk, w32, b32, out=out)
+                h_out.copy_(out, non_blocking=True)
+                torch.cuda.current_stream().synchronize()
+        else:
+            e2e_step = lambda: op.forward_f16_host(shape, h_x, h_off, h_msk, packed, b16, h_out,  # noqa: E731
+                                                   chunk_images=64)
         for _ in range(2):
             e2e_step()
         barrier(pg)
         torch.cuda.synchronize(dev)
         e_steps = max(1, min(args.steps, args.e2e_steps))
-        t0 = time.perf_counter()
         a = torch.cuda.Event(enable_timing=True)
         bev = torch.cuda.Event(enable_timing=True)
         a.record()
@@ -345,16 +409,17 @@ def run_ours(args):
         bev.synchronize()
         e_ms = max_over_ranks(a.elapsed_time(bev), pg) / e_steps
         op.device_error()
+        if not cfg["f32"]:
+            step()
+        torch.cuda.synchronize(dev)
         dev_out = h_out.to(dev)
-        ok = torch.equal(dev_out, out)
         mism = int((dev_out != out).sum().item())
-        maxdiff = float((dev_out.float() - out.float()).abs().max().item())
-        e2e = {"value": tiles * TILE_H * TILE_W / (e_ms * 1e-3) / 1e6, "unit": "Mpx/s",
-               "h2d_bytes_per_step": (h_x.numel() + h_off.numel() + h_msk.numel()) * 2,
-               "d2h_bytes_per_step": h_out.numel() * 2 + 4, "ms_per_step": e_ms, "steps": e_steps,
-               "matches_device_resident_output": bool(ok), "mismatched_outputs": mism,
-               "max_abs_diff_vs_device_resident": maxdiff, "per_rank_bytes": True}
-        del h_x, h_off, h_msk, h_out, one
+        e2e = {"value": job_px / (e_ms * 1e-3) / 1e6, "unit": "Mpx/s",
+               "h2d_bytes_per_step": (h_x.numel() + h_off.numel() + h_msk.numel()) * h_x.element_size(),
+               "d2h_bytes_per_step": h_out.numel() * h_out.element_size() + (0 if cfg["f32"] else 4),
+               "ms_per_step": e_ms, "steps": e_steps, "matches_device_resident_output": mism == 0,
+               "mismatched_outputs": mism, "per_rank_bytes": True}
+        del h_x, h_off, h_msk, h_out
 
     # ---- CPU baseline (rank 0, one GPU only) ----------------------------------------
     cpu = None
@@ -366,7 +431,8 @@ def run_ours(args):
         barrier(pg)
     if rank == 0:
         line = {
-            "metric": "DCNv2 output Mpixels/s (config 4: 2048 FP16 tiles 128x64x64->64, 3x3, 16 deformable groups)",
+            "metric": "DCNv2 output Mpixels/s (config 4: 2048 FP16 tiles 128x64x64->64, 3x3, 16 deformable groups)"
+            if args.config == 4 else f"DCNv2 output Mpixels/s ({cfg['desc'].split(':')[0]})",
             "value": value,
             "unit": "Mpx/s",
             "n_gpus": world,
@@ -374,27 +440,33 @@ def run_ours(args):
             "warmup": max(args.warmup, 3),
             "ms_per_step": ms_per_step,
             "higher_is_better": True,
-            "scaling": "strong",
+            "scaling": "strong" if cfg["sharded"] else "weak",
             "vs_baseline": None,
-            "dtype": "f16",
-            "data": "synthetic (seeded on device: x~N(0,1), offset 10*tanh(N(0,1))+flow U(-16,16), "
-                    "mask sigmoid(N(0,1)), Kaiming-uniform weights)",
-            "config": {"workload": f"config 4: N={tiles} tiles of 128x64x64 -> 64x64x64 FP16, 3x3, pad 1, "
-                                   "16 deformable groups, flow U(-16,16), sharded evenly over the GPUs",
-                       "tiles_per_gpu": t_end - t_begin, "px_per_gpu_step": px_per_step,
-                       "l2": "inputs > L2 every step (>1 GB per GPU per step); no flush needed",
-                       "parallelism": f"tile shards x{world}, no data-path collective"},
+            "dtype": "f32" if cfg["f32"] else "f16",
+            "data": "synthetic (seeded on device: x~N(0,1), offsets per config, mask sigmoid(N(0,1)), "
+                    "Kaiming-uniform weights)",
+            "config": {"workload": cfg["desc"] if args.config != 4 else cfg["desc"].replace("N=2048", f"N={total_images}"),
+                       "images_per_gpu": i_end - i_begin, "px_per_gpu_step": px_per_step,
+                       "path": {_native.DCN_PATH_SLAB_TC: "slab", _native.DCN_PATH_FUSED_TC: "global-gather"}.get(
+                           path, "direct"),
+                       "l2": ("inputs > L2 every step (>1 GB per GPU per step); no flush needed"
+                              if px_per_step * BYTES_PER_PX > 4 * 126e6 else
+                              "inputs fit in L2 and stay resident across steps (the reference's own repeated-launch "
+                              "setting for this config)"),
+                       "parallelism": (f"tile shards x{world}, no data-path collective" if cfg["sharded"] else
+                                       f"{world} independent replicas")},
             "roofline": {"bound": "hbm", "achieved": achieved_gbs, "peak": peaks["hbm_gbs"], "unit": "GB/s",
                          "frac": achieved_gbs / peaks["hbm_gbs"], "traffic": traffic,
                          "peak_source": f"{peak_kind} hbm_gbs", "kernel": kernel,
-                         "kernel_ms": fused_ms, "regroup_ms": regroup_ms,
-                         "algorithmic_bytes_per_px": BYTES_PER_PX,
-                         "tensor_tflops": tensor_tflops,
-                         "tensor_frac": tensor_tflops / peaks["bf16_tflops"],
+                         "kernel_ms": kernel_ms, "regroup_ms": regroup_ms,
+                         "algorithmic_bytes_per_px": bytes_per_px,
+                         "tensor_tflops": tensor_tflops if tensor_path else None,
+                         "tensor_frac": tensor_tflops / peaks["bf16_tflops"] if tensor_path else None,
                          "tensor_peak_source": f"{peak_kind} bf16_tflops (burst)"},
             "cpu_baseline": cpu,
             "e2e": e2e,
-            "gpu_launches": 2 * args.steps,
+            "raw_form": raw_form,
+            "gpu_launches": launches_per_step * args.steps,
             "clocks": clocks,
             "nonfinite_flag": nonfinite,
         }
@@ -410,7 +482,10 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
-    ap.add_argument("--tiles", type=int, default=TILES, help="total tiles (default: config 4's 2048)")
+    ap.add_argument("--config", type=int, default=4, choices=sorted(CONFIGS),
+                    help="benchmark configuration (default 4, the headline)")
+    ap.add_argument("--tiles", type=int, default=TILES, help="config 4: total tiles (default 2048)")
+    ap.add_argument("--no-raw", action="store_true", help="skip the fused offset-producer measurement")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--e2e-steps", type=int, default=5)
     ap.add_argument("--no-cpu-baseline", action="store_true")

@@ -265,6 +265,10 @@ class CudaDeformConv:
     def workspace_bytes(self, shape: DeformConvShape) -> int:
         return int(self.lib.dcn_forward_f16_workspace_bytes(ctypes.byref(shape.to_c())))
 
+    def raw_workspace_bytes(self, shape: DeformConvShape) -> int:
+        """Scratch of forward_f16_raw; 0 when the shape has no raw form (odd group count or direct path)."""
+        return int(self.lib.dcn_forward_f16_raw_workspace_bytes(ctypes.byref(shape.to_c())))
+
     # -- device-tensor API -----------------------------------------------------
     def _check_device(self, *tensors) -> None:
         for t in tensors:
@@ -383,7 +387,7 @@ class CudaDeformConv:
                 raise InvalidArrayCount(name, want, arr.numel())
         if out is None:
             out = torch.empty(shape.output_count, dtype=torch.float16, device=input.device)
-        ws_bytes = int(self.lib.dcn_forward_f16_raw_workspace_bytes(ctypes.byref(shape.to_c())))
+        ws_bytes = self.raw_workspace_bytes(shape)
         if ws_bytes == 0:
             raise Unsupported("shape does not take a tensor-core path with an even deformable-group count")
         if workspace is None:

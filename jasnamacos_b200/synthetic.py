@@ -176,6 +176,36 @@ def generate(config: int, tiles=None, batch: int | None = None, seed: int = CONF
     return inputs if config == 0 else inputs.quantized()
 
 
+def device_gaussian_batch(shape: DeformConvShape, seed: int, device, dtype=None, weight_seed: int = CONFIG_SEED):
+    """Config 0/1 distributions generated in device memory (x ~ N(0,1), offset ~ N(0, 2^2),
+    mask = sigmoid(N(0,1))), FP16 unless `dtype` says otherwise; weights/bias from `weights`."""
+    import torch
+
+    dtype = torch.float16 if dtype is None else dtype
+    g = torch.Generator(device=device)
+    g.manual_seed(seed)
+    x = torch.randn(shape.input_count, generator=g, device=device).to(dtype)
+    off = (2.0 * torch.randn(shape.offset_count, generator=g, device=device)).to(dtype)
+    msk = torch.sigmoid(torch.randn(shape.mask_count, generator=g, device=device)).to(dtype)
+    w, b = weights(shape, weight_seed)
+    return x, off, msk, w, b
+
+
+def device_raw_batch(shape: DeformConvShape, flow_range: float, seed: int, device):
+    """The offset network's raw output (2*G*9 residues ~ N(0,1), then G*9 mask logits ~ N(0,1))
+    and two flows ~ U(-flow_range, flow_range) in (x, y) order, FP16, in device memory."""
+    import torch
+
+    g = torch.Generator(device=device)
+    g.manual_seed(seed)
+    plane = shape.output_height * shape.output_width
+    gka = shape.offset_groups * shape.kernel_area
+    raw = torch.randn(shape.batch * 3 * gka * plane, generator=g, device=device).half()
+    f1 = ((torch.rand(shape.batch * 2 * plane, generator=g, device=device) * 2 - 1) * flow_range).half()
+    f2 = ((torch.rand(shape.batch * 2 * plane, generator=g, device=device) * 2 - 1) * flow_range).half()
+    return raw, f1, f2
+
+
 def device_batch(shape: DeformConvShape, flow_range: float, seed: int, device, weight_seed: int = CONFIG_SEED):
     """Config 2/3/4 distributions generated directly in device memory with torch's seeded
     generator (for benchmark batches too large to draw on the host).  Returns FP16 tensors
