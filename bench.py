@@ -238,6 +238,30 @@ def run_reference_arm(args):
 # ----------------------------------------------------------------------------- our arm
 
 
+def graphed(fn, enabled: bool):
+    """`fn` itself, or the replay of a CUDA graph that captured one call of it (for steps short
+    enough that the host's launch rate, not the GPU, would set the measured time)."""
+    if not enabled:
+        return fn
+    import torch
+
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        for _ in range(3):
+            fn()
+    torch.cuda.current_stream().wait_stream(side)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        fn()
+    torch.cuda.synchronize()
+    graphed.keep.append(graph)
+    return graph.replay
+
+
+graphed.keep = []
+
+
 def event_time_ms(fn, iters: int, stream=None) -> float:
     import torch
 
@@ -316,6 +340,8 @@ def run_ours(args):
         def step():
             op.forward_f16(shape, x, off, msk, packed, b16, out=out, flag=flag, workspace=ws)
     torch.cuda.synchronize(dev)
+    use_graph = args.graph == "on" or (args.graph == "auto" and not cfg["sharded"])
+    step = graphed(step, use_graph)
 
     # ---- device-resident throughput (the `value`) --------------------------------
     for _ in range(max(args.warmup, 3)):
@@ -343,9 +369,11 @@ def run_ours(args):
     regroup_ms = None
     if tensor_path:
         op.regroup_input(shape, x, workspace=ws)
-        kernel_ms = event_time_ms(lambda: op.forward_f16_grouped(shape, ws, off, msk, packed, b16, out=out, flag=flag),
+        kernel_ms = event_time_ms(graphed(lambda: op.forward_f16_grouped(shape, ws, off, msk, packed, b16, out=out,
+                                                                         flag=flag), use_graph),
                                   args.steps) / args.steps
-        regroup_ms = event_time_ms(lambda: op.regroup_input(shape, x, workspace=ws), args.steps) / args.steps
+        regroup_ms = event_time_ms(graphed(lambda: op.regroup_input(shape, x, workspace=ws), use_graph),
+                                   args.steps) / args.steps
         launches_per_step = 2
     else:
         kernel_ms = ms / args.steps
@@ -365,8 +393,8 @@ def run_ours(args):
     if tensor_path and not args.no_raw and op.raw_workspace_bytes(shape) > 0:
         raw, f1, f2 = synthetic.device_raw_batch(shape, cfg["flow"] or 16.0, seed=2000 + i_begin, device=dev)
         wsr = torch.empty(op.raw_workspace_bytes(shape), dtype=torch.uint8, device=dev)
-        raw_step = lambda: op.forward_f16_raw(shape, x, raw, f1, f2, packed, b16, out=out, flag=flag,  # noqa: E731
-                                              workspace=wsr)
+        raw_step = graphed(lambda: op.forward_f16_raw(shape, x, raw, f1, f2, packed, b16, out=out, flag=flag,
+                                                      workspace=wsr), use_graph)
         for _ in range(3):
             raw_step()
         barrier(pg)
@@ -454,7 +482,8 @@ def run_ours(args):
                               "inputs fit in L2 and stay resident across steps (the reference's own repeated-launch "
                               "setting for this config)"),
                        "parallelism": (f"tile shards x{world}, no data-path collective" if cfg["sharded"] else
-                                       f"{world} independent replicas")},
+                                       f"{world} independent replicas"),
+                       "launch": "CUDA graph replay per step" if use_graph else "direct launches per step"},
             "roofline": {"bound": "hbm", "achieved": achieved_gbs, "peak": peaks["hbm_gbs"], "unit": "GB/s",
                          "frac": achieved_gbs / peaks["hbm_gbs"], "traffic": traffic,
                          "peak_source": f"{peak_kind} hbm_gbs", "kernel": kernel,
@@ -471,6 +500,7 @@ def run_ours(args):
             "nonfinite_flag": nonfinite,
         }
         print(json.dumps(line), flush=True)
+    graphed.keep.clear()
     if pg is not None:
         pg.destroy_process_group()
     return 0
@@ -486,6 +516,8 @@ def main():
                     help="benchmark configuration (default 4, the headline)")
     ap.add_argument("--tiles", type=int, default=TILES, help="config 4: total tiles (default 2048)")
     ap.add_argument("--no-raw", action="store_true", help="skip the fused offset-producer measurement")
+    ap.add_argument("--graph", choices=("auto", "on", "off"), default="auto",
+                    help="time steps as CUDA graph replays (auto: for the single-image configs 0, 1, 3)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--e2e-steps", type=int, default=5)
     ap.add_argument("--no-cpu-baseline", action="store_true")

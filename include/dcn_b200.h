@@ -227,6 +227,44 @@ dcn_status dcn_forward_f16_raw(const dcn_shape *shape, const void *input, const 
                                const void *bias, void *output, uint32_t *nonfinite_flag,
                                void *workspace, size_t workspace_bytes, dcn_stream stream);
 
+/* ---- tensor plumbing: split input, output slot --------------------------------
+ * Where the FP16 operator reads its input channels and writes its output channels,
+ * for callers whose tensors are not exactly [N][C][H][W] in / [N][OC][Ho][Wo] out:
+ *  - input_second != NULL: `input` holds channels [0, input_split) as
+ *    [N][input_split][H][W] and input_second holds [input_split, C) as
+ *    [N][C - input_split][H][W].  This replaces the deformInput = [feat_prop, feat_n2]
+ *    concatenation of assemble_temporal_alignment_fp16 (MetalShader.swift:769-813):
+ *    the two 64-channel features are read in place.  On the tensor-core paths
+ *    input_split must be a multiple of 8 (one deformable group never straddles the
+ *    two tensors); the direct path takes any split in [1, C-1].  With
+ *    input_second == NULL, input_split must be 0.
+ *  - output_image_channels != 0: the output tensor has output_image_channels
+ *    channels per image and the operator writes channels
+ *    [output_channel_offset, output_channel_offset + OC) of it, leaving the others
+ *    untouched.  This replaces the copy of the aligned feature into the backbone
+ *    input of assemble_temporal_backbone_fp16 (MetalShader.swift:903-929; slot
+ *    64 * (branch + 1) of a 64 * (branch + 2)-channel tensor).  With
+ *    output_image_channels == 0 the output is the plain [N][OC][Ho][Wo] and
+ *    output_channel_offset must be 0.
+ * A NULL dcn_io means all defaults (dcn_forward_f16 and dcn_forward_f16_raw pass NULL).
+ * Invalid combinations return DCN_ERR_INVALID_ARGUMENT. */
+typedef struct dcn_io {
+    const void *input_second;
+    int32_t input_split;
+    int32_t output_image_channels;
+    int32_t output_channel_offset;
+} dcn_io;
+
+dcn_status dcn_forward_f16_io(const dcn_shape *shape, const dcn_io *io, const void *input,
+                              const void *offset, const void *mask, const void *packed_weight,
+                              const void *bias, void *output, uint32_t *nonfinite_flag,
+                              void *workspace, size_t workspace_bytes, dcn_stream stream);
+dcn_status dcn_forward_f16_raw_io(const dcn_shape *shape, const dcn_io *io, const void *input,
+                                  const void *raw, const void *flow1, const void *flow2,
+                                  const void *packed_weight, const void *bias, void *output,
+                                  uint32_t *nonfinite_flag, void *workspace, size_t workspace_bytes,
+                                  dcn_stream stream);
+
 /* ---- non-finite detection -----------------------------------------------------
  * flag_non_finite_fp16 (MetalShader.swift:454-463): ORs DCN_FLAG_NONFINITE into
  * *flag if any of `count` FP16 values is Inf or NaN. */

@@ -70,8 +70,20 @@ class DcnCounts(ctypes.Structure):
     _fields_ = [(name, ctypes.c_int64) for name in ("input", "offset", "mask", "weight", "bias", "output")]
 
 
+class DcnIo(ctypes.Structure):
+    """`struct dcn_io`: split input tensors and the output slot (null pointer = defaults)."""
+
+    _fields_ = [
+        ("input_second", ctypes.c_void_p),
+        ("input_split", ctypes.c_int32),
+        ("output_image_channels", ctypes.c_int32),
+        ("output_channel_offset", ctypes.c_int32),
+    ]
+
+
 _P = ctypes.c_void_p
 _SHAPE = ctypes.POINTER(DcnShape)
+_IO = ctypes.POINTER(DcnIo)
 
 # Every entry point of include/dcn_b200.h: name -> (restype, argtypes).
 PROTOTYPES = {
@@ -100,6 +112,14 @@ PROTOTYPES = {
     "dcn_forward_f16_raw": (
         ctypes.c_int,
         [_SHAPE, _P, _P, _P, _P, _P, _P, _P, _P, _P, ctypes.c_size_t, _P],
+    ),
+    "dcn_forward_f16_io": (
+        ctypes.c_int,
+        [_SHAPE, _IO, _P, _P, _P, _P, _P, _P, _P, _P, ctypes.c_size_t, _P],
+    ),
+    "dcn_forward_f16_raw_io": (
+        ctypes.c_int,
+        [_SHAPE, _IO, _P, _P, _P, _P, _P, _P, _P, _P, _P, ctypes.c_size_t, _P],
     ),
     "dcn_flag_non_finite_f16": (ctypes.c_int, [_P, ctypes.c_int64, _P, _P]),
     "dcn_prepare_offsets_f16": (ctypes.c_int, [ctypes.c_int64, _P, _P, _P, _P, _P, _P]),

@@ -20,12 +20,15 @@ namespace dcn {
 
 cudaError_t launch_direct_f32(const Params &p, const float *input, const float *offset, const float *mask,
                               const float *weight, const float *bias, float *output, cudaStream_t stream);
-cudaError_t launch_direct_f16(const Params &p, const __half *input, const __half *offset, const __half *mask,
-                              const __half *weight, const __half *bias, __half *output, cudaStream_t stream);
+cudaError_t launch_direct_f16(const Params &p, const SplitInput<__half> &input, const __half *offset,
+                              const __half *mask, const __half *weight, const __half *bias, __half *output,
+                              cudaStream_t stream);
 cudaError_t launch_prepack_weights(const Params &p, bool fused, int kb, const void *src, dcn_dtype src_dtype,
                                    int layout, void *dst, cudaStream_t stream);
 cudaError_t launch_flag_non_finite(const __half *values, int64_t count, uint32_t *flag, int sm_count,
                                    cudaStream_t stream);
+cudaError_t launch_flag_non_finite_rows(const __half *values, int64_t rows, int64_t row_len, int64_t row_stride,
+                                        uint32_t *flag, int sm_count, cudaStream_t stream);
 cudaError_t launch_prepare_offsets(int64_t n_images, int gka, int64_t plane, const __half *raw, const __half *flow1,
                                    const __half *flow2, __half *offset, __half *mask, cudaStream_t stream);
 cudaError_t launch_slab_grouped_raw(const Params &p, const void *slabs, const __half *raw, const __half *flow1,
@@ -36,7 +39,8 @@ bool fused_supported(const Params &p);
 int fused_kblocks(const Params &p);
 size_t fused_workspace_bytes(const Params &p);
 cudaError_t fused_prepare_device(uint32_t **err_word);
-cudaError_t launch_regroup_c8(const Params &p, const __half *input, void *workspace, cudaStream_t stream);
+cudaError_t launch_regroup_c8(const Params &p, const SplitInput<__half> &input, void *workspace,
+                              cudaStream_t stream);
 cudaError_t launch_fused_grouped(const Params &p, const void *input_c8, const __half *offset, const __half *mask,
                                  const uint8_t *packed_w, const __half *bias, __half *output, uint32_t *flag,
                                  int sm_count, uint32_t *err, cudaStream_t stream);
@@ -44,7 +48,8 @@ bool slab_supported(const Params &p);
 size_t slab_workspace_bytes(const Params &p);
 size_t slab_packed_weight_bytes(const Params &p);
 cudaError_t slab_prepare_device();
-cudaError_t launch_regroup_slabs(const Params &p, const __half *input, void *workspace, cudaStream_t stream);
+cudaError_t launch_regroup_slabs(const Params &p, const SplitInput<__half> &input, void *workspace,
+                                 cudaStream_t stream);
 cudaError_t launch_prepack_slab(const Params &p, const void *src, dcn_dtype src_dtype, int layout, void *dst,
                                 cudaStream_t stream);
 cudaError_t launch_slab_grouped(const Params &p, const void *slabs, const __half *offset, const __half *mask,
@@ -244,8 +249,9 @@ dcn_status dcn_forward_f16_direct(const dcn_shape *shape, const void *input, con
         return DCN_ERR_INVALID_ARGUMENT;
     DeviceInfo *dev = nullptr;
     if ((st = current_device(&dev)) != DCN_OK) return st;
+    const Params p = make_params(*shape);
     return from_cuda(launch_direct_f16(
-        make_params(*shape), static_cast<const __half *>(input), static_cast<const __half *>(offset),
+        p, SplitInput<__half>{static_cast<const __half *>(input), nullptr, p.C, p.C}, static_cast<const __half *>(offset),
         static_cast<const __half *>(mask), static_cast<const __half *>(weight_oihw),
         static_cast<const __half *>(bias), static_cast<__half *>(output), reinterpret_cast<cudaStream_t>(stream)));
 }
@@ -314,37 +320,68 @@ dcn_status launch_grouped(dcn_path path, const Params &p, const void *grouped, c
     return from_cuda(launch_fused_grouped(p, grouped, off, msk, w, b, out, flag, dev->sm_count, dev->err_word, s));
 }
 
-cudaError_t launch_regroup(dcn_path path, const Params &p, const void *input, void *workspace, cudaStream_t s) {
-    const auto *in = static_cast<const __half *>(input);
+cudaError_t launch_regroup(dcn_path path, const Params &p, const SplitInput<__half> &in, void *workspace,
+                           cudaStream_t s) {
     return path == DCN_PATH_SLAB_TC ? launch_regroup_slabs(p, in, workspace, s) : launch_regroup_c8(p, in, workspace, s);
+}
+
+// Applies a caller's dcn_io (null: defaults) to the kernel parameters and builds the
+// input view.  The output slot goes into p (out_ct, out_c0).
+dcn_status resolve_io(const dcn_io *io, dcn_path path, const void *input, Params *p, SplitInput<__half> *in) {
+    *in = SplitInput<__half>{static_cast<const __half *>(input), nullptr, p->C, p->C};
+    if (io == nullptr) return DCN_OK;
+    if (io->input_second != nullptr) {
+        const int split = io->input_split;
+        if (split <= 0 || split >= p->C || !aligned(io->input_second, 2)) return DCN_ERR_INVALID_ARGUMENT;
+        // The regroup pre-passes read one deformable group's 8 channels from one tensor.
+        if (path != DCN_PATH_DIRECT && split % 8 != 0) return DCN_ERR_INVALID_ARGUMENT;
+        in->second = static_cast<const __half *>(io->input_second);
+        in->split = split;
+    } else if (io->input_split != 0) {
+        return DCN_ERR_INVALID_ARGUMENT;
+    }
+    if (io->output_image_channels == 0) {
+        if (io->output_channel_offset != 0) return DCN_ERR_INVALID_ARGUMENT;
+    } else {
+        if (io->output_channel_offset < 0 ||
+            static_cast<int64_t>(io->output_image_channels) < static_cast<int64_t>(p->OC) + io->output_channel_offset)
+            return DCN_ERR_INVALID_ARGUMENT;
+        p->out_ct = io->output_image_channels;
+        p->out_c0 = io->output_channel_offset;
+    }
+    return DCN_OK;
 }
 
 }  // namespace
 
-dcn_status dcn_forward_f16(const dcn_shape *shape, const void *input, const void *offset, const void *mask,
-                           const void *packed_weight, const void *bias, void *output, uint32_t *nonfinite_flag,
-                           void *workspace, size_t workspace_bytes, dcn_stream stream) {
+dcn_status dcn_forward_f16_io(const dcn_shape *shape, const dcn_io *io, const void *input, const void *offset,
+                              const void *mask, const void *packed_weight, const void *bias, void *output,
+                              uint32_t *nonfinite_flag, void *workspace, size_t workspace_bytes,
+                              dcn_stream stream) {
     dcn_status st = validate(shape);
     if (st != DCN_OK) return st;
     if (!input || !offset || !mask || !packed_weight || !bias || !output) return DCN_ERR_INVALID_ARGUMENT;
     if (!aligned(input, 2) || !aligned(bias, 2) || !aligned(output, 2) || !aligned(packed_weight, 16) ||
         (nonfinite_flag && !aligned(nonfinite_flag, 4)))
         return DCN_ERR_INVALID_ARGUMENT;
+    Params p = make_params(*shape);
+    const dcn_path path = select_path(p);
+    SplitInput<__half> in;
+    if ((st = resolve_io(io, path, input, &p, &in)) != DCN_OK) return st;
     DeviceInfo *dev = nullptr;
     if ((st = current_device(&dev)) != DCN_OK) return st;
-    const Params p = make_params(*shape);
     cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-    const dcn_path path = select_path(p);
     if (path == DCN_PATH_DIRECT) {
         if (!aligned(offset, 2) || !aligned(mask, 2)) return DCN_ERR_INVALID_ARGUMENT;
-        cudaError_t e = launch_direct_f16(p, static_cast<const __half *>(input),
-                                          static_cast<const __half *>(offset), static_cast<const __half *>(mask),
+        cudaError_t e = launch_direct_f16(p, in, static_cast<const __half *>(offset),
+                                          static_cast<const __half *>(mask),
                                           static_cast<const __half *>(packed_weight),
                                           static_cast<const __half *>(bias), static_cast<__half *>(output), s);
         if (e == cudaSuccess && nonfinite_flag)
-            e = launch_flag_non_finite(static_cast<const __half *>(output),
-                                       static_cast<int64_t>(p.N) * p.OC * p.out_plane, nonfinite_flag,
-                                       dev->sm_count, s);
+            e = launch_flag_non_finite_rows(static_cast<const __half *>(output) + output_index(p, 0, 0, 0), p.N,
+                                            static_cast<int64_t>(p.OC) * p.out_plane,
+                                            static_cast<int64_t>(p.out_ct) * p.out_plane, nonfinite_flag,
+                                            dev->sm_count, s);
         return from_cuda(e);
     }
     // Tensor-core paths: offsets/masks are read by TMA (16-byte aligned rows), the
@@ -352,9 +389,16 @@ dcn_status dcn_forward_f16(const dcn_shape *shape, const void *input, const void
     if (!aligned(offset, 16) || !aligned(mask, 16)) return DCN_ERR_INVALID_ARGUMENT;
     if (!workspace || !aligned(workspace, 256) || workspace_bytes < dcn_forward_f16_workspace_bytes(shape))
         return DCN_ERR_INVALID_ARGUMENT;
-    cudaError_t e = launch_regroup(path, p, input, workspace, s);
+    cudaError_t e = launch_regroup(path, p, in, workspace, s);
     if (e != cudaSuccess) return from_cuda(e);
     return launch_grouped(path, p, workspace, offset, mask, packed_weight, bias, output, nonfinite_flag, dev, s);
+}
+
+dcn_status dcn_forward_f16(const dcn_shape *shape, const void *input, const void *offset, const void *mask,
+                           const void *packed_weight, const void *bias, void *output, uint32_t *nonfinite_flag,
+                           void *workspace, size_t workspace_bytes, dcn_stream stream) {
+    return dcn_forward_f16_io(shape, nullptr, input, offset, mask, packed_weight, bias, output, nonfinite_flag,
+                              workspace, workspace_bytes, stream);
 }
 
 dcn_status dcn_regroup_input_f16(const dcn_shape *shape, const void *input, void *workspace,
@@ -369,7 +413,8 @@ dcn_status dcn_regroup_input_f16(const dcn_shape *shape, const void *input, void
         return DCN_ERR_INVALID_ARGUMENT;
     DeviceInfo *dev = nullptr;
     if ((st = current_device(&dev)) != DCN_OK) return st;
-    return from_cuda(launch_regroup(path, p, input, workspace, reinterpret_cast<cudaStream_t>(stream)));
+    const SplitInput<__half> in{static_cast<const __half *>(input), nullptr, p.C, p.C};
+    return from_cuda(launch_regroup(path, p, in, workspace, reinterpret_cast<cudaStream_t>(stream)));
 }
 
 dcn_status dcn_forward_f16_grouped(const dcn_shape *shape, const void *input_grouped, const void *offset,
@@ -433,13 +478,13 @@ size_t dcn_forward_f16_raw_workspace_bytes(const dcn_shape *shape) {
     return path == DCN_PATH_SLAB_TC ? base : base + offset_bytes(p) + mask_bytes(p);
 }
 
-dcn_status dcn_forward_f16_raw(const dcn_shape *shape, const void *input, const void *raw, const void *flow1,
-                               const void *flow2, const void *packed_weight, const void *bias, void *output,
-                               uint32_t *nonfinite_flag, void *workspace, size_t workspace_bytes,
-                               dcn_stream stream) {
+dcn_status dcn_forward_f16_raw_io(const dcn_shape *shape, const dcn_io *io, const void *input, const void *raw,
+                                  const void *flow1, const void *flow2, const void *packed_weight, const void *bias,
+                                  void *output, uint32_t *nonfinite_flag, void *workspace, size_t workspace_bytes,
+                                  dcn_stream stream) {
     dcn_status st = validate(shape);
     if (st != DCN_OK) return st;
-    const Params p = make_params(*shape);
+    Params p = make_params(*shape);
     const dcn_path path = select_path(p);
     if (path == DCN_PATH_DIRECT || p.OG % 2 != 0) return DCN_ERR_UNSUPPORTED;
     if (!input || !raw || !flow1 || !flow2 || !packed_weight || !bias || !output) return DCN_ERR_INVALID_ARGUMENT;
@@ -449,13 +494,15 @@ dcn_status dcn_forward_f16_raw(const dcn_shape *shape, const void *input, const 
         return DCN_ERR_INVALID_ARGUMENT;
     if (!workspace || !aligned(workspace, 256) || workspace_bytes < dcn_forward_f16_raw_workspace_bytes(shape))
         return DCN_ERR_INVALID_ARGUMENT;
+    SplitInput<__half> in;
+    if ((st = resolve_io(io, path, input, &p, &in)) != DCN_OK) return st;
     DeviceInfo *dev = nullptr;
     if ((st = current_device(&dev)) != DCN_OK) return st;
     cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
     const auto *r = static_cast<const __half *>(raw);
     const auto *f1 = static_cast<const __half *>(flow1);
     const auto *f2 = static_cast<const __half *>(flow2);
-    cudaError_t e = launch_regroup(path, p, input, workspace, s);
+    cudaError_t e = launch_regroup(path, p, in, workspace, s);
     if (e != cudaSuccess) return from_cuda(e);
     if (path == DCN_PATH_SLAB_TC)
         return from_cuda(launch_slab_grouped_raw(p, workspace, r, f1, f2, static_cast<const uint8_t *>(packed_weight),
@@ -469,6 +516,14 @@ dcn_status dcn_forward_f16_raw(const dcn_shape *shape, const void *input, const 
     e = launch_prepare_offsets(p.N, p.OG * p.KA, p.out_plane, r, f1, f2, offset, mask, s);
     if (e != cudaSuccess) return from_cuda(e);
     return launch_grouped(path, p, workspace, offset, mask, packed_weight, bias, output, nonfinite_flag, dev, s);
+}
+
+dcn_status dcn_forward_f16_raw(const dcn_shape *shape, const void *input, const void *raw, const void *flow1,
+                               const void *flow2, const void *packed_weight, const void *bias, void *output,
+                               uint32_t *nonfinite_flag, void *workspace, size_t workspace_bytes,
+                               dcn_stream stream) {
+    return dcn_forward_f16_raw_io(shape, nullptr, input, raw, flow1, flow2, packed_weight, bias, output,
+                                  nonfinite_flag, workspace, workspace_bytes, stream);
 }
 
 dcn_status dcn_device_error(void) {

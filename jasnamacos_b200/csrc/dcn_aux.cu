@@ -14,12 +14,15 @@ namespace dcn {
 
 namespace {
 
-__global__ void flag_non_finite_kernel(const __half *__restrict__ values, int64_t count,
-                                       uint32_t *__restrict__ flag) {
+// `rows` runs of `row_len` values, `row_stride` apart (one run per image of an output
+// slot inside a larger tensor; rows = 1 for a plain array).
+__global__ void flag_non_finite_kernel(const __half *__restrict__ values, int64_t rows, int64_t row_len,
+                                       int64_t row_stride, uint32_t *__restrict__ flag) {
     bool bad = false;
+    const int64_t count = rows * row_len;
     for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < count;
          i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-        const __half h = values[i];
+        const __half h = values[(i / row_len) * row_stride + i % row_len];
         bad |= __hisinf(h) != 0 || __hisnan(h);
     }
     if (__any_sync(0xffffffffu, bad) && (threadIdx.x % 32) == 0) atomicOr(flag, DCN_FLAG_NONFINITE);
@@ -53,14 +56,20 @@ __global__ void prepare_offsets_kernel(int64_t n_images, int gka, int64_t plane,
 
 }  // namespace
 
-cudaError_t launch_flag_non_finite(const __half *values, int64_t count, uint32_t *flag, int sm_count,
-                                   cudaStream_t stream) {
-    int64_t blocks = (count + 255) / 256;
+cudaError_t launch_flag_non_finite_rows(const __half *values, int64_t rows, int64_t row_len, int64_t row_stride,
+                                        uint32_t *flag, int sm_count, cudaStream_t stream) {
+    int64_t blocks = (rows * row_len + 255) / 256;
     const int64_t cap = static_cast<int64_t>(sm_count) * 8;
     if (blocks > cap) blocks = cap;
     if (blocks < 1) blocks = 1;
-    flag_non_finite_kernel<<<static_cast<unsigned>(blocks), 256, 0, stream>>>(values, count, flag);
+    flag_non_finite_kernel<<<static_cast<unsigned>(blocks), 256, 0, stream>>>(values, rows, row_len, row_stride,
+                                                                               flag);
     return cudaGetLastError();
+}
+
+cudaError_t launch_flag_non_finite(const __half *values, int64_t count, uint32_t *flag, int sm_count,
+                                   cudaStream_t stream) {
+    return launch_flag_non_finite_rows(values, 1, count, count, flag, sm_count, stream);
 }
 
 cudaError_t launch_prepare_offsets(int64_t n_images, int gka, int64_t plane, const __half *raw, const __half *flow1,

@@ -25,6 +25,8 @@ struct Params {
     int KA;                // kernel area KH*KW
     int in_plane;          // H*W
     int out_plane;         // HO*WO
+    int out_ct;            // channels per image of the output tensor (>= out_c0 + OC)
+    int out_c0;            // first output-tensor channel this operator writes
 };
 
 inline Params make_params(const dcn_shape &s) {
@@ -39,8 +41,30 @@ inline Params make_params(const dcn_shape &s) {
     p.KA = p.KH * p.KW;
     p.in_plane = p.H * p.W;
     p.out_plane = p.HO * p.WO;
+    p.out_ct = p.OC;
+    p.out_c0 = 0;
     return p;
 }
+
+// Element offset of output (n, oc, spatial) in the caller's output tensor, which may hold
+// more channels per image than this operator writes (out_ct, starting at out_c0).
+__host__ __device__ inline int64_t output_index(const Params &p, int64_t n, int oc, int64_t spatial) {
+    return (n * p.out_ct + p.out_c0 + oc) * static_cast<int64_t>(p.out_plane) + spatial;
+}
+
+// NCHW input whose channels may live in two tensors: channels [0, split) in `first`
+// ([N][split][H][W]) and [split, C) in `second` ([N][C - split][H][W]).  With one
+// tensor, second is null and split == C.
+template <typename T>
+struct SplitInput {
+    const T *first;
+    const T *second;
+    int split;
+    int C;
+    __host__ __device__ const T *channel(int64_t n, int c, int64_t plane) const {
+        return c < split ? first + (n * split + c) * plane : second + (n * (C - split) + (c - split)) * plane;
+    }
+};
 
 // Longest any device-side wait may spin before it gives up and reports
 // DCN_ERR_DEVICE_TIMEOUT (nanoseconds of %globaltimer).

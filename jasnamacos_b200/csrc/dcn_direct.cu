@@ -61,7 +61,7 @@ __device__ __forceinline__ float sample_exact(const T *plane, int H, int W, floa
 // Dynamic shared memory: chunk_ic * KA * 32 floats.
 template <typename T>
 __global__ void __launch_bounds__(kThreads)
-    direct_kernel(Params p, const T *__restrict__ input, const T *__restrict__ offset,
+    direct_kernel(Params p, const SplitInput<T> input, const T *__restrict__ offset,
                   const T *__restrict__ mask, const T *__restrict__ weight,
                   const T *__restrict__ bias, T *__restrict__ output, int chunk_ic) {
     extern __shared__ float s_samples[];  // [chunk_ic][KA][kPix]
@@ -112,7 +112,7 @@ __global__ void __launch_bounds__(kThreads)
                 const float off_x = load_val(offset, obase + static_cast<int64_t>(offset_channel + 1) * p.out_plane + spatial);
                 const float y = __fadd_rn(static_cast<float>(oy * p.SH - p.PH + ky * p.DH), off_y);
                 const float x = __fadd_rn(static_cast<float>(ox * p.SW - p.PW + kx * p.DW), off_x);
-                const T *plane = input + (static_cast<int64_t>(n) * p.C + ic) * p.in_plane;
+                const T *plane = input.channel(n, ic, p.in_plane);
                 const float sampled = sample_exact(plane, p.H, p.W, y, x);
                 const int64_t mbase = static_cast<int64_t>(n) * p.OG * p.KA * p.out_plane;
                 const float m = load_val(mask, mbase + static_cast<int64_t>(og * p.KA + k) * p.out_plane + spatial);
@@ -148,7 +148,7 @@ __global__ void __launch_bounds__(kThreads)
             const int oc_local = oc_block * kOcPerBlock + oc_lane + kOcLanes * j;
             if (oc_local < p.opg) {
                 const int oc = group * p.opg + oc_local;
-                store_val(output, (static_cast<int64_t>(my_n) * p.OC + oc) * p.out_plane + my_spatial, acc[j]);
+                store_val(output, output_index(p, my_n, oc, my_spatial), acc[j]);
             }
         }
     }
@@ -164,7 +164,7 @@ int chunk_channels(const Params &p) {
 }
 
 template <typename T>
-cudaError_t launch_direct(const Params &p, const T *input, const T *offset, const T *mask,
+cudaError_t launch_direct(const Params &p, const SplitInput<T> &input, const T *offset, const T *mask,
                           const T *weight, const T *bias, T *output, cudaStream_t stream) {
     const int chunk = chunk_channels(p);
     const size_t smem = static_cast<size_t>(chunk) * p.KA * kPix * sizeof(float);
@@ -185,10 +185,11 @@ cudaError_t launch_direct(const Params &p, const T *input, const T *offset, cons
 cudaError_t launch_direct_f32(const Params &p, const float *input, const float *offset,
                               const float *mask, const float *weight, const float *bias,
                               float *output, cudaStream_t stream) {
-    return launch_direct<float>(p, input, offset, mask, weight, bias, output, stream);
+    return launch_direct<float>(p, SplitInput<float>{input, nullptr, p.C, p.C}, offset, mask, weight, bias, output,
+                                stream);
 }
 
-cudaError_t launch_direct_f16(const Params &p, const __half *input, const __half *offset,
+cudaError_t launch_direct_f16(const Params &p, const SplitInput<__half> &input, const __half *offset,
                               const __half *mask, const __half *weight, const __half *bias,
                               __half *output, cudaStream_t stream) {
     return launch_direct<__half>(p, input, offset, mask, weight, bias, output, stream);

@@ -266,7 +266,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int n = tile / a.tiles_per_image;
             const int px = (tile % a.tiles_per_image) * BM + r;
             if (px < p.out_plane) {
-                __half *dst = a.out + static_cast<size_t>(n) * BN * p.out_plane + px;
+                __half *dst = a.out + output_index(p, n, 0, px);
 #pragma unroll
                 for (int oc = 0; oc < BN; ++oc) {
                     const __half h = __float2half_rn(__uint_as_float(v[oc]) + s.bias[oc]);
@@ -413,31 +413,36 @@ __global__ void __launch_bounds__(kThreads, 1)
 // each half zero where the column is outside the image.  A bilinear sample whose
 // left corner is column x0 (-1 <= x0 <= W-1) then reads its two corners of one
 // row with a single aligned 32-byte load of entry x0+1.
-__global__ void __launch_bounds__(256) regroup_pairs_kernel(const __half *__restrict__ in,
-                                                             uint4 *__restrict__ out, int C, int H, int W,
-                                                             int64_t total) {
-    const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;  // entry index
-    if (i >= total) return;
-    const int e = static_cast<int>(i % (W + 1));
-    const int64_t rest = i / (W + 1);
-    const int y = static_cast<int>(rest % H);
-    const int64_t ng = rest / H;  // n * (C/8) + g
+// Grid: x over the H (W+1) entries of one group plane, y = group g, z strides over the
+// images n (so no 64-bit division per thread).
+__global__ void __launch_bounds__(256) regroup_pairs_kernel(const SplitInput<__half> in,
+                                                             uint4 *__restrict__ out, int N, int H, int W) {
+    const int entries = H * (W + 1);
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;  // entry index within the plane
+    if (i >= entries) return;
+    const int g = blockIdx.y;
+    const int groups = gridDim.y;
+    const int y = i / (W + 1);
+    const int e = i - y * (W + 1);
     const int64_t plane = static_cast<int64_t>(H) * W;
-    const __half *src = in + ng * 8 * plane + static_cast<int64_t>(y) * W;
     const __half zero = __float2half_rn(0.0f);
-    uint32_t w[8];
+    for (int64_t n = blockIdx.z; n < N; n += gridDim.z) {
+        const __half *src = in.channel(n, g * 8, plane) + static_cast<int64_t>(y) * W;
+        uint32_t w[8];
 #pragma unroll
-    for (int half_sel = 0; half_sel < 2; ++half_sel) {
-        const int x = e - 1 + half_sel;
-        const bool in_row = x >= 0 && x < W;
-        __half h[8];
+        for (int half_sel = 0; half_sel < 2; ++half_sel) {
+            const int x = e - 1 + half_sel;
+            const bool in_row = x >= 0 && x < W;
+            __half h[8];
 #pragma unroll
-        for (int c = 0; c < 8; ++c) h[c] = in_row ? src[c * plane + x] : zero;
+            for (int c = 0; c < 8; ++c) h[c] = in_row ? src[c * plane + x] : zero;
 #pragma unroll
-        for (int c = 0; c < 4; ++c) w[half_sel * 4 + c] = pack_half2(__halves2half2(h[2 * c], h[2 * c + 1]));
+            for (int c = 0; c < 4; ++c) w[half_sel * 4 + c] = pack_half2(__halves2half2(h[2 * c], h[2 * c + 1]));
+        }
+        const int64_t o = ((n * groups + g) * entries + i) * 2;
+        out[o] = make_uint4(w[0], w[1], w[2], w[3]);
+        out[o + 1] = make_uint4(w[4], w[5], w[6], w[7]);
     }
-    out[2 * i] = make_uint4(w[0], w[1], w[2], w[3]);
-    out[2 * i + 1] = make_uint4(w[4], w[5], w[6], w[7]);
 }
 
 // ---------------------------------------------------------------- host side
@@ -515,10 +520,12 @@ cudaError_t fused_prepare_device(uint32_t **err_word) {
 }
 
 // NCHW FP16 -> corner pairs (the layout the fused kernel gathers from).
-cudaError_t launch_regroup_c8(const Params &p, const __half *input, void *workspace, cudaStream_t stream) {
-    const int64_t total = static_cast<int64_t>(p.N) * (p.C / 8) * p.H * (p.W + 1);
-    fused::regroup_pairs_kernel<<<static_cast<unsigned>((total + 255) / 256), 256, 0, stream>>>(
-        input, static_cast<uint4 *>(workspace), p.C, p.H, p.W, total);
+cudaError_t launch_regroup_c8(const Params &p, const SplitInput<__half> &input, void *workspace,
+                              cudaStream_t stream) {
+    const int entries = p.H * (p.W + 1);
+    const dim3 grid(static_cast<unsigned>((entries + 255) / 256), static_cast<unsigned>(p.C / 8),
+                    static_cast<unsigned>(p.N < 65535 ? p.N : 65535));
+    fused::regroup_pairs_kernel<<<grid, 256, 0, stream>>>(input, static_cast<uint4 *>(workspace), p.N, p.H, p.W);
     return cudaGetLastError();
 }
 

@@ -341,7 +341,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (lane == 0) mbar_arrive(&s.acc_empty[t]);
                 const int px = (t0 + t) * BM + r;
                 if (px < p.out_plane) {
-                    __half *dst = a.out + static_cast<size_t>(n) * BN * p.out_plane + px;
+                    __half *dst = a.out + output_index(p, n, 0, px);
 #pragma unroll
                     for (int oc = 0; oc < BN; ++oc) {
                         const __half h = __float2half_rn(__uint_as_float(v[oc]) + s.bias[oc]);
@@ -500,29 +500,87 @@ __global__ void __launch_bounds__(kThreads, 1)
 // NCHW FP16 -> zero-bordered slabs [N][C/8][H+2][W+2][8]: slab (n, g) holds the 8
 // channels of deformable group g at every position, 16 bytes per position, with a
 // one-pixel ring of zeros so bilinear corners just outside the image read zero.
-__global__ void __launch_bounds__(256) regroup_slabs_kernel(const __half *__restrict__ in, uint4 *__restrict__ out,
-                                                             int C, int H, int W, int64_t total) {
-    const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;  // padded position index
-    if (i >= total) return;
+// Grid: x over the (H+2)(W+2) padded positions of one slab, y = group g, z strides
+// over the images n (so no 64-bit division per thread).
+__global__ void __launch_bounds__(256) regroup_slabs_kernel(const SplitInput<__half> in, uint4 *__restrict__ out,
+                                                             int N, int H, int W) {
     const int sw = W + 2;
-    const int px = static_cast<int>(i % sw);
-    const int64_t rest = i / sw;
-    const int py = static_cast<int>(rest % (H + 2));
-    const int64_t ng = rest / (H + 2);  // n * (C/8) + g
-    const int y = py - 1, x = px - 1;
-    uint4 o = make_uint4(0u, 0u, 0u, 0u);
-    if (y >= 0 && y < H && x >= 0 && x < W) {
-        const int64_t plane = static_cast<int64_t>(H) * W;
-        const __half *src = in + ng * 8 * plane + static_cast<int64_t>(y) * W + x;
-        __half h[8];
+    const int positions = (H + 2) * sw;
+    const int pos = blockIdx.x * blockDim.x + threadIdx.x;
+    if (pos >= positions) return;
+    const int g = blockIdx.y;
+    const int groups = gridDim.y;
+    const int py = pos / sw;
+    const int y = py - 1, x = pos - py * sw - 1;
+    const bool inside = y >= 0 && y < H && x >= 0 && x < W;
+    const int64_t plane = static_cast<int64_t>(H) * W;
+    for (int64_t n = blockIdx.z; n < N; n += gridDim.z) {
+        uint4 o = make_uint4(0u, 0u, 0u, 0u);
+        if (inside) {
+            const __half *src = in.channel(n, g * 8, plane) + static_cast<int64_t>(y) * W + x;
+            __half h[8];
 #pragma unroll
-        for (int c = 0; c < 8; ++c) h[c] = src[c * plane];
-        o.x = pack_half2(__halves2half2(h[0], h[1]));
-        o.y = pack_half2(__halves2half2(h[2], h[3]));
-        o.z = pack_half2(__halves2half2(h[4], h[5]));
-        o.w = pack_half2(__halves2half2(h[6], h[7]));
+            for (int c = 0; c < 8; ++c) h[c] = src[c * plane];
+            o.x = pack_half2(__halves2half2(h[0], h[1]));
+            o.y = pack_half2(__halves2half2(h[2], h[3]));
+            o.z = pack_half2(__halves2half2(h[4], h[5]));
+            o.w = pack_half2(__halves2half2(h[6], h[7]));
+        }
+        out[(n * groups + g) * positions + pos] = o;
     }
-    out[i] = o;
+}
+
+// The same transform, four source columns per thread: 8-byte loads of 4 consecutive
+// pixels from each of the group's 8 channel planes, transposed in registers into four
+// 16-byte slab positions.  Needs W % 4 == 0 and 8-byte aligned channel planes.  Thread
+// j < W/4 of padded row py writes positions 4j+1 .. 4j+4; thread j == W/4 writes the
+// two border columns 0 and W+1; the border rows 0 and H+1 are all zeros.
+__global__ void __launch_bounds__(256) regroup_slabs_x4_kernel(const SplitInput<__half> in, uint4 *__restrict__ out,
+                                                                int N, int H, int W) {
+    const int per_row = W / 4 + 1;
+    const int t = blockIdx.x * blockDim.x + threadIdx.x;
+    if (t >= (H + 2) * per_row) return;
+    const int g = blockIdx.y;
+    const int groups = gridDim.y;
+    const int py = t / per_row;
+    const int j = t - py * per_row;
+    const int sw = W + 2;
+    const int positions = (H + 2) * sw;
+    const int64_t plane = static_cast<int64_t>(H) * W;
+    const bool interior_row = py >= 1 && py <= H;
+    const uint4 zero = make_uint4(0u, 0u, 0u, 0u);
+    for (int64_t n = blockIdx.z; n < N; n += gridDim.z) {
+        uint4 *row = out + (n * groups + g) * positions + static_cast<int64_t>(py) * sw;
+        if (j == W / 4) {
+            row[0] = zero;
+            row[W + 1] = zero;
+            continue;
+        }
+        uint4 o[4] = {zero, zero, zero, zero};
+        if (interior_row) {
+            const __half *src = in.channel(n, g * 8, plane) + static_cast<int64_t>(py - 1) * W + 4 * j;
+            uint2 v[8];
+#pragma unroll
+            for (int c = 0; c < 8; ++c) v[c] = *reinterpret_cast<const uint2 *>(src + c * plane);
+            // v[c] holds pixels 4j..4j+3 of channel c as half pairs (x, y); position i
+            // needs channel pairs (0,1) (2,3) (4,5) (6,7) of pixel i.
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const int w = i >> 1;
+                const uint32_t sel = (i & 1) ? 0x7632u : 0x5410u;  // high or low halves
+                uint32_t r[4];
+#pragma unroll
+                for (int c2 = 0; c2 < 4; ++c2) {
+                    const uint32_t a = w ? v[2 * c2].y : v[2 * c2].x;
+                    const uint32_t b = w ? v[2 * c2 + 1].y : v[2 * c2 + 1].x;
+                    r[c2] = __byte_perm(a, b, sel);
+                }
+                o[i] = make_uint4(r[0], r[1], r[2], r[3]);
+            }
+        }
+#pragma unroll
+        for (int i = 0; i < 4; ++i) row[4 * j + 1 + i] = o[i];
+    }
 }
 
 // Weights -> per-group SW32 K-major B blocks.  Group g, block kk (K = 16: taps 2kk,
@@ -590,10 +648,22 @@ cudaError_t slab_prepare_device() {
                                 static_cast<int>(smem));
 }
 
-cudaError_t launch_regroup_slabs(const Params &p, const __half *input, void *workspace, cudaStream_t stream) {
-    const int64_t total = static_cast<int64_t>(p.N) * (p.C / 8) * (p.H + 2) * (p.W + 2);
-    slab::regroup_slabs_kernel<<<static_cast<unsigned>((total + 255) / 256), 256, 0, stream>>>(
-        input, static_cast<uint4 *>(workspace), p.C, p.H, p.W, total);
+cudaError_t launch_regroup_slabs(const Params &p, const SplitInput<__half> &input, void *workspace,
+                                 cudaStream_t stream) {
+    const unsigned images = static_cast<unsigned>(p.N < 65535 ? p.N : 65535);
+    const int64_t plane = static_cast<int64_t>(p.H) * p.W;
+    const bool vec = p.W % 4 == 0 && plane % 4 == 0 && (reinterpret_cast<uintptr_t>(input.first) & 7u) == 0 &&
+                     (input.second == nullptr || (reinterpret_cast<uintptr_t>(input.second) & 7u) == 0);
+    if (vec) {
+        const int threads = (p.H + 2) * (p.W / 4 + 1);
+        const dim3 grid(static_cast<unsigned>((threads + 255) / 256), static_cast<unsigned>(p.C / 8), images);
+        slab::regroup_slabs_x4_kernel<<<grid, 256, 0, stream>>>(input, static_cast<uint4 *>(workspace), p.N, p.H,
+                                                                 p.W);
+    } else {
+        const int positions = (p.H + 2) * (p.W + 2);
+        const dim3 grid(static_cast<unsigned>((positions + 255) / 256), static_cast<unsigned>(p.C / 8), images);
+        slab::regroup_slabs_kernel<<<grid, 256, 0, stream>>>(input, static_cast<uint4 *>(workspace), p.N, p.H, p.W);
+    }
     return cudaGetLastError();
 }
 

@@ -322,25 +322,60 @@ class CudaDeformConv:
         raise_for_status(st, "dcn_prepack_weights")
         return packed
 
+    @staticmethod
+    def _io(shape, input, input_second, out_image_channels, out_channel_offset):
+        """The dcn_io of a call and the element counts of its input/output tensors."""
+        if input_second is None and out_image_channels is None and out_channel_offset == 0:
+            return None, shape.input_count, shape.output_count
+        plane = shape.input_height * shape.input_width
+        io = _native.DcnIo()
+        in_count = shape.input_count
+        if input_second is not None:
+            first_ch = input.numel() // (shape.batch * plane)
+            second_ch = input_second.numel() // (shape.batch * plane)
+            if first_ch + second_ch != shape.input_channels or first_ch * shape.batch * plane != input.numel():
+                raise InvalidArrayCount("input + input_second", shape.input_count,
+                                        input.numel() + input_second.numel())
+            io.input_second = _ptr(input_second)
+            io.input_split = first_ch
+            in_count = input.numel()
+        out_count = shape.output_count
+        if out_image_channels is not None:
+            io.output_image_channels = out_image_channels
+            io.output_channel_offset = out_channel_offset
+            out_count = shape.batch * out_image_channels * shape.output_height * shape.output_width
+        else:
+            io.output_channel_offset = out_channel_offset
+        return io, in_count, out_count
+
     def forward_f16(self, shape, input, offset, mask, packed_weight, bias, out=None, flag=None,
-                    workspace=None, stream=None):
+                    workspace=None, stream=None, input_second=None, out_image_channels=None,
+                    out_channel_offset=0):
         """Fused FP16 DCNv2 (gather + tcgen05 GEMM + epilogue); replaces the reference's
-        gather + SIMD-group GEMM + non-finite-flag passes (MetalShader.swift:299-463)."""
+        gather + SIMD-group GEMM + non-finite-flag passes (MetalShader.swift:299-463).
+
+        `input_second` (channels [split, C) of the input, `input` then holding [0, split))
+        and `out_image_channels`/`out_channel_offset` (write channels [offset, offset+OC) of
+        an output tensor with that many channels per image) read and write the caller's
+        tensors in place, as dcn_forward_f16_io does."""
         torch = _torch()
-        for name, arr, want in (("input", input, shape.input_count), ("offset", offset, shape.offset_count),
+        io, in_count, out_count = self._io(shape, input, input_second, out_image_channels, out_channel_offset)
+        for name, arr, want in (("input", input, in_count), ("offset", offset, shape.offset_count),
                                 ("mask", mask, shape.mask_count), ("bias", bias, shape.output_channels)):
             if arr.numel() != want:
                 raise InvalidArrayCount(name, want, arr.numel())
         if out is None:
-            out = torch.empty(shape.output_count, dtype=torch.float16, device=input.device)
+            out = torch.empty(out_count, dtype=torch.float16, device=input.device)
+        elif out.numel() != out_count:
+            raise InvalidArrayCount("output", out_count, out.numel())
         ws_bytes = self.workspace_bytes(shape)
         if workspace is None and ws_bytes > 0:
             workspace = torch.empty(ws_bytes, dtype=torch.uint8, device=input.device)
-        self._check_device(input, offset, mask, packed_weight, bias, out, flag, workspace)
+        self._check_device(input, input_second, offset, mask, packed_weight, bias, out, flag, workspace)
         with torch.cuda.device(input.device):
-            st = self.lib.dcn_forward_f16(
-                ctypes.byref(shape.to_c()), _ptr(input), _ptr(offset), _ptr(mask), _ptr(packed_weight),
-                _ptr(bias), _ptr(out), _ptr(flag), _ptr(workspace),
+            st = self.lib.dcn_forward_f16_io(
+                ctypes.byref(shape.to_c()), None if io is None else ctypes.byref(io), _ptr(input), _ptr(offset),
+                _ptr(mask), _ptr(packed_weight), _ptr(bias), _ptr(out), _ptr(flag), _ptr(workspace),
                 0 if workspace is None else workspace.numel() * workspace.element_size(), _stream_handle(stream))
         raise_for_status(st, "dcn_forward_f16")
         return out
@@ -373,29 +408,35 @@ class CudaDeformConv:
         return out
 
     def forward_f16_raw(self, shape, input, raw, flow1, flow2, packed_weight, bias, out=None, flag=None,
-                        workspace=None, stream=None):
+                        workspace=None, stream=None, input_second=None, out_image_channels=None,
+                        out_channel_offset=0):
         """Offset producer + DCNv2 in one operator: `raw` is the offset network's output
         [N][3*G*9][Ho][Wo] (residues, then mask logits), flows [N][2][Ho][Wo] in (x, y) order;
-        replaces prepare_dcn_offsets_fp16 (MetalShader.swift:817-839) followed by the convolution."""
+        replaces prepare_dcn_offsets_fp16 (MetalShader.swift:817-839) followed by the convolution.
+        The tensor-plumbing arguments are those of forward_f16 (dcn_forward_f16_raw_io)."""
         torch = _torch()
+        io, in_count, out_count = self._io(shape, input, input_second, out_image_channels, out_channel_offset)
         gka = shape.offset_groups * shape.kernel_area
         plane = shape.output_height * shape.output_width
-        for name, arr, want in (("input", input, shape.input_count), ("raw", raw, shape.batch * 3 * gka * plane),
+        for name, arr, want in (("input", input, in_count), ("raw", raw, shape.batch * 3 * gka * plane),
                                 ("flow1", flow1, shape.batch * 2 * plane), ("flow2", flow2, shape.batch * 2 * plane),
                                 ("bias", bias, shape.output_channels)):
             if arr.numel() != want:
                 raise InvalidArrayCount(name, want, arr.numel())
         if out is None:
-            out = torch.empty(shape.output_count, dtype=torch.float16, device=input.device)
+            out = torch.empty(out_count, dtype=torch.float16, device=input.device)
+        elif out.numel() != out_count:
+            raise InvalidArrayCount("output", out_count, out.numel())
         ws_bytes = self.raw_workspace_bytes(shape)
         if ws_bytes == 0:
             raise Unsupported("shape does not take a tensor-core path with an even deformable-group count")
         if workspace is None:
             workspace = torch.empty(ws_bytes, dtype=torch.uint8, device=input.device)
-        self._check_device(input, raw, flow1, flow2, packed_weight, bias, out, flag, workspace)
+        self._check_device(input, input_second, raw, flow1, flow2, packed_weight, bias, out, flag, workspace)
         with torch.cuda.device(input.device):
-            st = self.lib.dcn_forward_f16_raw(
-                ctypes.byref(shape.to_c()), _ptr(input), _ptr(raw), _ptr(flow1), _ptr(flow2), _ptr(packed_weight),
+            st = self.lib.dcn_forward_f16_raw_io(
+                ctypes.byref(shape.to_c()), None if io is None else ctypes.byref(io), _ptr(input), _ptr(raw),
+                _ptr(flow1), _ptr(flow2), _ptr(packed_weight),
                 _ptr(bias), _ptr(out), _ptr(flag), _ptr(workspace), workspace.numel() * workspace.element_size(),
                 _stream_handle(stream))
         raise_for_status(st, "dcn_forward_f16_raw")

@@ -117,3 +117,37 @@ def test_null_pointers_are_rejected_before_any_device_work(lib):
     assert lib.dcn_prepack_weights(ctypes.byref(s), None, 0, 0, None, None) == _native.DCN_ERR_INVALID_ARGUMENT
     assert lib.dcn_flag_non_finite_f16(None, 4, None, None) == _native.DCN_ERR_INVALID_ARGUMENT
     assert lib.dcn_prepare_offsets_f16(0, None, None, None, None, None, None) == _native.DCN_ERR_INVALID_SHAPE
+
+
+def test_io_plumbing_is_validated_before_device_work(lib):
+    """dcn_io rules (split on an 8-channel boundary for the tensor-core paths, the slot inside
+    the output tensor) are checked before the device is touched: here, without a GPU, a valid
+    dcn_io gets as far as DCN_ERR_NO_DEVICE and an invalid one stops at DCN_ERR_INVALID_ARGUMENT."""
+    import torch
+
+    if torch.cuda.is_available():
+        pytest.skip("checks the no-device status")
+    s = DeformConvShape.jasna_propagation().to_c()
+    p = ctypes.c_void_p(256)
+
+    def call(io):
+        return lib.dcn_forward_f16_io(ctypes.byref(s), io, p, p, p, p, p, p, None, p, 1 << 30, None)
+
+    def raw_call(io):
+        return lib.dcn_forward_f16_raw_io(ctypes.byref(s), io, p, p, p, p, p, p, p, None, p, 1 << 30, None)
+
+    second = ctypes.c_void_p(512)
+    for good in (None, _native.DcnIo(second, 64, 0, 0), _native.DcnIo(None, 0, 192, 128),
+                 _native.DcnIo(second, 8, 64, 0)):
+        arg = None if good is None else ctypes.byref(good)
+        assert call(arg) == _native.DCN_ERR_NO_DEVICE
+        assert raw_call(arg) == _native.DCN_ERR_NO_DEVICE
+    for bad in (_native.DcnIo(second, 60, 0, 0),     # not a deformable-group boundary
+                _native.DcnIo(second, 0, 0, 0),      # empty first part
+                _native.DcnIo(second, 128, 0, 0),    # empty second part
+                _native.DcnIo(None, 64, 0, 0),       # split without a second tensor
+                _native.DcnIo(None, 0, 0, 5),        # offset without a channel count
+                _native.DcnIo(None, 0, 100, 40),     # slot past the end of the tensor
+                _native.DcnIo(None, 0, 192, -1)):
+        assert call(ctypes.byref(bad)) == _native.DCN_ERR_INVALID_ARGUMENT
+        assert raw_call(ctypes.byref(bad)) == _native.DCN_ERR_INVALID_ARGUMENT

@@ -217,10 +217,13 @@ def test_prepack_sources_agree(cuda_op, tmp_path):
 
 
 def test_ragged_tiles_and_small_planes(cuda_op):
-    """Planes that are not a multiple of the 128-pixel tile (fused, masked last tile) and planes
-    that are not a multiple of 8 (direct path)."""
-    for h, w_, n in ((12, 20, 3), (10, 36, 2), (5, 5, 2), (3, 7, 1)):
+    """Planes that are not a multiple of the 128-pixel tile (fused, masked last tile), widths that
+    are not a multiple of 4 (the slab pre-pass's one-column form), and planes that are not a
+    multiple of 8 (direct path)."""
+    for h, w_, n in ((12, 20, 3), (10, 36, 2), (8, 9, 2), (16, 6, 1), (5, 5, 2), (3, 7, 1)):
         s = DeformConvShape.jasna_propagation(n, h, w_)
+        want = _native.DCN_PATH_DIRECT if (h * w_) % 8 else _native.DCN_PATH_SLAB_TC
+        assert cuda_op.path(s) == want, (h, w_)
         g = synthetic.SplitMix64(h * 100 + w_)
         arrays = [synthetic.quantize_f16(a) for a in (
             g.normal(s.input_count), g.uniform(s.offset_count, -4, 4), g.uniform(s.mask_count, 0, 1),
