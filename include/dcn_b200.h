@@ -201,11 +201,19 @@ dcn_status dcn_forward_f16(const dcn_shape *shape, const void *input, const void
  *   selected path in `workspace` (dcn_forward_f16_workspace_bytes bytes): 8 channels
  *   of one deformable group per 16 bytes, as zero-bordered per-group slabs
  *   (DCN_PATH_SLAB_TC) or as 32-byte horizontal corner pairs (DCN_PATH_FUSED_TC).
- * dcn_forward_f16_grouped: the tensor-core kernel reading such an input (16-byte
- *   aligned).  Both return DCN_ERR_UNSUPPORTED for DCN_PATH_DIRECT shapes. */
+ * dcn_forward_f16_grouped: the tensor-core kernel reading such an input from the
+ *   start of a workspace (16-byte aligned, dcn_forward_f16_workspace_bytes bytes): on
+ *   the slab path, batches with fewer 128-pixel tiles than the B200 has SMs split the
+ *   deformable groups across SMs and keep FP32 partial sums in the workspace past the
+ *   regrouped input, then add them in a fixed order in a second launch.  Results are
+ *   deterministic for a shape; an image computed in a split batch can differ from the
+ *   same image in a large batch by one FP16 rounding step (another FP32 summation
+ *   order).  DCN_B200_GROUP_SPLIT=0 in the environment (read once per process) turns
+ *   the split off, making every image's result independent of its batch.
+ * Both return DCN_ERR_UNSUPPORTED for DCN_PATH_DIRECT shapes. */
 dcn_status dcn_regroup_input_f16(const dcn_shape *shape, const void *input, void *workspace,
                                  size_t workspace_bytes, dcn_stream stream);
-dcn_status dcn_forward_f16_grouped(const dcn_shape *shape, const void *input_grouped,
+dcn_status dcn_forward_f16_grouped(const dcn_shape *shape, void *input_grouped,
                                    const void *offset, const void *mask, const void *packed_weight,
                                    const void *bias, void *output, uint32_t *nonfinite_flag,
                                    dcn_stream stream);

@@ -417,7 +417,7 @@ dcn_status dcn_regroup_input_f16(const dcn_shape *shape, const void *input, void
     return from_cuda(launch_regroup(path, p, in, workspace, reinterpret_cast<cudaStream_t>(stream)));
 }
 
-dcn_status dcn_forward_f16_grouped(const dcn_shape *shape, const void *input_grouped, const void *offset,
+dcn_status dcn_forward_f16_grouped(const dcn_shape *shape, void *input_grouped, const void *offset,
                                    const void *mask, const void *packed_weight, const void *bias, void *output,
                                    uint32_t *nonfinite_flag, dcn_stream stream) {
     dcn_status st = validate(shape);

@@ -19,6 +19,12 @@
 //           the MMA thread issues 5 MMAs (K = 80) into the tile's accumulator
 //   4 epilogue warps drain each tile's accumulator after its last group.
 //
+// Batches too small to give every SM a unit (one image: 32 tiles on 148 SMs) split
+// the deformable groups too: a unit then covers one tile and 1/s of the groups, its
+// epilogue writes the FP32 partial sum to the workspace, and slab_reduce_kernel adds
+// the s partials in a fixed order (bias, FP16, NCHW, Inf/NaN flag).  s depends only on
+// the shape (slab_group_splits), so the result of a shape is the same on every run.
+//
 // Compared with gathering from global memory this trades the random 32-byte L1
 // requests (one data-pipe wavefront per lane, ~500 cycles) for random 16-byte
 // shared loads (~2.5 wavefronts per 8 lanes, ~30 cycles), and reads each input
@@ -27,6 +33,8 @@
 // Every mbarrier wait is bounded (kWaitLimitNs); a timeout sets the device error
 // word, stops the CTA's warps, drains in-flight copies and MMAs and frees TMEM.
 #include <cuda.h>
+#include <cstdlib>
+#include <string>
 #include <cuda_fp16.h>
 #include <cudaTypedefs.h>
 
@@ -91,8 +99,27 @@ struct Args {
     int tiles_per_image;
     int tiles_per_unit;        // 1..4
     int units_per_image;
-    int num_units;
+    int splits;                // group ranges per tile set (1: no split)
+    int groups_per_split;      // OG / splits
+    int num_units;             // N * units_per_image * splits
+    float *partial;            // splits > 1: [splits][N][BN][plane] FP32 partial sums
 };
+
+// Work unit u: image n, first tile t0, tile count mt, first deformable group g0.
+struct Unit {
+    int n, t0, mt, g0;
+};
+
+__device__ __forceinline__ Unit decode_unit(const Args &a, int u) {
+    Unit w;
+    const int j = u % a.splits;
+    const int rest = u / a.splits;
+    w.n = rest / a.units_per_image;
+    w.t0 = (rest % a.units_per_image) * a.tiles_per_unit;
+    w.mt = min(a.tiles_per_unit, a.tiles_per_image - w.t0);
+    w.g0 = j * a.groups_per_split;
+    return w;
+}
 
 __device__ __forceinline__ uint32_t pack_half2(__half2 h) { return *reinterpret_cast<uint32_t *>(&h); }
 
@@ -205,10 +232,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             uint32_t gi = 0, si = 0;
             bool ok = true;
             for (int u = blockIdx.x; u < a.num_units && ok; u += gridDim.x) {
-                const int n = u / a.units_per_image;
-                const int t0 = (u % a.units_per_image) * a.tiles_per_unit;
-                const int mt = min(a.tiles_per_unit, a.tiles_per_image - t0);
-                for (int g = 0; g < OG && ok; ++g, ++gi) {
+                const Unit w = decode_unit(a, u);
+                const int n = w.n, t0 = w.t0, mt = w.mt;
+                for (int g = w.g0; g < w.g0 + a.groups_per_split && ok; ++g, ++gi) {
                     const uint32_t gb = gi & 1u, gph = (gi >> 1) & 1u;
                     if (!mbar_wait_bounded(&s.grp_empty[gb], gph ^ 1u, abort_flag)) {
                         signal_abort(s, a.err);
@@ -262,9 +288,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             uint32_t last_parity = 0;
             bool ok = true;
             for (int u = blockIdx.x; u < a.num_units && ok; u += gridDim.x) {
-                const int t0 = (u % a.units_per_image) * a.tiles_per_unit;
-                const int mt = min(a.tiles_per_unit, a.tiles_per_image - t0);
-                for (int g = 0; g < OG && ok; ++g, ++gi) {
+                const Unit w = decode_unit(a, u);
+                const int mt = w.mt, g_last = w.g0 + a.groups_per_split - 1;
+                for (int g = w.g0; g <= g_last && ok; ++g, ++gi) {
                     const uint32_t gb = gi & 1u, gph = (gi >> 1) & 1u;
                     if (!mbar_wait_bounded(&s.grp_full[gb], gph, abort_flag)) {
                         signal_abort(s, a.err);
@@ -273,7 +299,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     }
                     const uint32_t b_base = smem_addr(s.b[gb]);
                     for (int t = 0; t < mt; ++t, ++si) {
-                        if (g == 0) {
+                        if (g == w.g0) {
                             if (!mbar_wait_bounded(&s.acc_empty[t], (uses[t] & 1u) ^ 1u, abort_flag)) {
                                 signal_abort(s, a.err);
                                 ok = false;
@@ -292,12 +318,12 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
                         for (int kk = 0; kk < kMmasPerStage; ++kk) {
                             const uint64_t bdesc = make_sw32_kmajor_desc(b_base + kk * kBBlockBytes);
-                            umma_f16_ts(d_tmem, a_tmem + kk * 8, bdesc, idesc, (g | kk) != 0 ? 1u : 0u);
+                            umma_f16_ts(d_tmem, a_tmem + kk * 8, bdesc, idesc, (g != w.g0 || kk != 0) ? 1u : 0u);
                         }
                         umma_commit(&s.a_empty[st]);
                         last_bar = &s.a_empty[st];
                         last_parity = ph;
-                        if (g == OG - 1) {
+                        if (g == g_last) {
                             umma_commit(&s.acc_full[t]);
                             last_bar = &s.acc_full[t];
                             last_parity = uses[t] & 1u;
@@ -320,9 +346,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         bool nonfinite = false;
         bool ok = true;
         for (int u = blockIdx.x; u < a.num_units && ok; u += gridDim.x) {
-            const int n = u / a.units_per_image;
-            const int t0 = (u % a.units_per_image) * a.tiles_per_unit;
-            const int mt = min(a.tiles_per_unit, a.tiles_per_image - t0);
+            const Unit w = decode_unit(a, u);
+            const int n = w.n, t0 = w.t0, mt = w.mt;
             for (int t = 0; t < mt; ++t) {
                 if (!mbar_wait_bounded(&s.acc_full[t], uses[t] & 1u, abort_flag, kIdleBackoffNs)) {
                     signal_abort(s, a.err);
@@ -340,7 +365,18 @@ __global__ void __launch_bounds__(kThreads, 1)
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&s.acc_empty[t]);
                 const int px = (t0 + t) * BM + r;
-                if (px < p.out_plane) {
+                if (a.partial != nullptr) {
+                    // Group split: this unit's FP32 partial sum; bias, FP16 and the flag
+                    // come in slab_reduce_kernel.
+                    if (px < p.out_plane) {
+                        const int split = w.g0 / a.groups_per_split;
+                        float *dst = a.partial +
+                                     ((static_cast<int64_t>(split) * p.N + n) * BN) * p.out_plane + px;
+#pragma unroll
+                        for (int oc = 0; oc < BN; ++oc)
+                            dst[static_cast<int64_t>(oc) * p.out_plane] = __uint_as_float(v[oc]);
+                    }
+                } else if (px < p.out_plane) {
                     __half *dst = a.out + output_index(p, n, 0, px);
 #pragma unroll
                     for (int oc = 0; oc < BN; ++oc) {
@@ -374,8 +410,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         uint32_t gi = 0, si = 0;
         bool ok = true;
         for (int u = blockIdx.x; u < a.num_units && ok; u += gridDim.x) {
-            const int t0 = (u % a.units_per_image) * a.tiles_per_unit;
-            const int mt = min(a.tiles_per_unit, a.tiles_per_image - t0);
+            const Unit w = decode_unit(a, u);
+            const int t0 = w.t0, mt = w.mt;
             // Per tile of the unit: this pixel's integer sampling base (oy*SH - PH,
             // ox*SW - PW) as floats, and whether the pixel exists (its samples are
             // skipped, and its A row left zero, when it is past the output plane).
@@ -390,7 +426,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 bfy[t] = static_cast<float>(oy * p.SH - p.PH);
                 bfx[t] = static_cast<float>(ox * p.SW - p.PW);
             }
-            for (int g = 0; g < OG && ok; ++g, ++gi) {
+            for (int g = 0; g < a.groups_per_split && ok; ++g, ++gi) {
                 const uint32_t gb = gi & 1u, gph = (gi >> 1) & 1u;
                 if (!mbar_wait_bounded(&s.grp_full[gb], gph, abort_flag)) {
                     ok = false;
@@ -530,6 +566,40 @@ __global__ void __launch_bounds__(256) regroup_slabs_kernel(const SplitInput<__h
     }
 }
 
+// Group split, second pass: out[n][oc][px] = FP16(bias[oc] + partial[0] + ... +
+// partial[s-1]) summed in split order, four pixels per thread, with the Inf/NaN flag.
+__global__ void __launch_bounds__(256) slab_reduce_kernel(Params p, const float *__restrict__ partial, int splits,
+                                                           const __half *__restrict__ bias, __half *__restrict__ out,
+                                                           uint32_t *__restrict__ flag) {
+    const int64_t per_split = static_cast<int64_t>(p.N) * BN * p.out_plane;
+    const int64_t i = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) * 4;
+    bool bad = false;
+    if (i < per_split) {
+        const int64_t row = i / p.out_plane;  // n * BN + oc
+        const int px = static_cast<int>(i - row * p.out_plane);
+        const int oc = static_cast<int>(row % BN);
+        const int64_t n = row / BN;
+        float4 acc = *reinterpret_cast<const float4 *>(partial + i);
+        for (int j = 1; j < splits; ++j) {
+            const float4 v = *reinterpret_cast<const float4 *>(partial + j * per_split + i);
+            acc.x += v.x;
+            acc.y += v.y;
+            acc.z += v.z;
+            acc.w += v.w;
+        }
+        const float b = __half2float(bias[oc]);
+        const __half h[4] = {__float2half_rn(acc.x + b), __float2half_rn(acc.y + b), __float2half_rn(acc.z + b),
+                             __float2half_rn(acc.w + b)};
+        __half *dst = out + output_index(p, n, oc, px);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            bad |= __hisinf(h[k]) != 0 || __hisnan(h[k]);
+            dst[k] = h[k];
+        }
+    }
+    if (flag != nullptr && __any_sync(0xffffffffu, bad) && (threadIdx.x % 32) == 0) atomicOr(flag, DCN_FLAG_NONFINITE);
+}
+
 // The same transform, four source columns per thread: 8-byte loads of 4 consecutive
 // pixels from each of the group's 8 channel planes, transposed in registers into four
 // 16-byte slab positions.  Needs W % 4 == 0 and 8-byte aligned channel planes.  Thread
@@ -625,9 +695,45 @@ bool slab_supported(const Params &p) {
     return true;
 }
 
-size_t slab_workspace_bytes(const Params &p) {
+namespace {
+
+// B200 SM count: the unit count the group split aims for.  A fixed number rather than
+// the device's, so that the split (and with it the summation order and the workspace
+// size) depends on the shape alone.
+constexpr int kSplitTargetUnits = 148;
+
+size_t slab_slabs_bytes(const Params &p) {
     const size_t bytes = static_cast<size_t>(p.N) * p.OG * (p.H + 2) * (p.W + 2) * 16;
     return (bytes + 255) & ~size_t{255};
+}
+
+}  // namespace
+
+// DCN_B200_GROUP_SPLIT=0 turns the split off for the process (read once), for callers
+// that need an image's result to be bit-identical whatever batch it is computed in.
+bool group_split_allowed() {
+    static const bool allowed = [] {
+        const char *v = std::getenv("DCN_B200_GROUP_SPLIT");
+        return !(v != nullptr && std::string(v) == "0");
+    }();
+    return allowed;
+}
+
+// Deformable-group split of a shape: the largest power of two s <= OG dividing OG with
+// (tiles in the batch) x s <= kSplitTargetUnits; 1 for batches that already fill the GPU.
+int slab_group_splits(const Params &p) {
+    if (!group_split_allowed()) return 1;
+    const int64_t tiles = static_cast<int64_t>(p.N) * ((p.out_plane + slab::BM - 1) / slab::BM);
+    int splits = 1;
+    while (splits * 2 <= p.OG && p.OG % (splits * 2) == 0 && tiles * splits * 2 <= kSplitTargetUnits) splits *= 2;
+    return splits;
+}
+
+size_t slab_workspace_bytes(const Params &p) {
+    const int splits = slab_group_splits(p);
+    size_t bytes = slab_slabs_bytes(p);
+    if (splits > 1) bytes += static_cast<size_t>(splits) * p.N * slab::BN * p.out_plane * sizeof(float);
+    return bytes;
 }
 
 size_t slab_packed_weight_bytes(const Params &p) { return static_cast<size_t>(p.OG) * slab::kBGroupBytes; }
@@ -704,12 +810,29 @@ slab::Args make_slab_args(const Params &p, const void *slabs, const uint8_t *pac
     a.tiles_per_image = (p.out_plane + BM - 1) / BM;
     // Up to 4 tiles per work unit (each unit reads every group's slab once); fewer
     // when that would leave SMs idle.
+    a.splits = slab_group_splits(p);
+    a.groups_per_split = p.OG / a.splits;
     int tpu = kMaxTilesPerUnit;
-    while (tpu > 1 && static_cast<int64_t>(p.N) * ((a.tiles_per_image + tpu - 1) / tpu) < 2 * sm_count) tpu /= 2;
+    while (tpu > 1 && (a.splits > 1 ||
+                       static_cast<int64_t>(p.N) * ((a.tiles_per_image + tpu - 1) / tpu) < 2 * sm_count))
+        tpu /= 2;
     a.tiles_per_unit = tpu;
     a.units_per_image = (a.tiles_per_image + tpu - 1) / tpu;
-    a.num_units = p.N * a.units_per_image;
+    a.num_units = p.N * a.units_per_image * a.splits;
+    a.partial = a.splits > 1
+                    ? reinterpret_cast<float *>(const_cast<uint8_t *>(a.slabs) + slab_slabs_bytes(p))
+                    : nullptr;
     return a;
+}
+
+// The second pass of a group-split launch (nothing when the shape is not split).
+cudaError_t launch_split_reduce(const Params &p, const slab::Args &a, cudaStream_t stream) {
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess || a.splits == 1) return e;
+    const int64_t quads = static_cast<int64_t>(p.N) * slab::BN * p.out_plane / 4;
+    slab::slab_reduce_kernel<<<static_cast<unsigned>((quads + 255) / 256), 256, 0, stream>>>(p, a.partial, a.splits,
+                                                                                             a.bias, a.out, a.flag);
+    return cudaGetLastError();
 }
 
 }  // namespace
@@ -725,7 +848,7 @@ cudaError_t launch_slab_grouped(const Params &p, const void *slabs, const __half
     const Args a = make_slab_args(p, slabs, packed_w, bias, output, flag, sm_count, err);
     const int grid = a.num_units < sm_count ? a.num_units : sm_count;
     slab_dcn_kernel<false><<<grid, kThreads, slab_smem_bytes(p), stream>>>(tmap_off, tmap_msk, tmap_off, tmap_msk, a);
-    return cudaGetLastError();
+    return launch_split_reduce(p, a, stream);
 }
 
 // raw: [N][3*OG*KA][plane] (offset residues, then mask logits); flow1/flow2: [N][2][plane].
@@ -744,7 +867,7 @@ cudaError_t launch_slab_grouped_raw(const Params &p, const void *slabs, const __
     const Args a = make_slab_args(p, slabs, packed_w, bias, output, flag, sm_count, err);
     const int grid = a.num_units < sm_count ? a.num_units : sm_count;
     slab_dcn_kernel<true><<<grid, kThreads, slab_smem_bytes(p), stream>>>(tmap_off, tmap_msk, tmap_f1, tmap_f2, a);
-    return cudaGetLastError();
+    return launch_split_reduce(p, a, stream);
 }
 
 }  // namespace dcn

@@ -78,8 +78,13 @@ def test_path_selection_and_sizes(lib):
     # 64x64 tiles take the shared-memory slab kernel by default.
     assert lib.dcn_forward_f16_path(ctypes.byref(jasna)) == _native.DCN_PATH_SLAB_TC
     assert lib.dcn_packed_weight_bytes(ctypes.byref(jasna)) == 16 * 5 * 2048  # 16 groups x 5 SW32 blocks
-    # zero-bordered slabs: (C/8) groups x (H+2) x (W+2) positions x 16 bytes
-    assert lib.dcn_forward_f16_workspace_bytes(ctypes.byref(jasna)) == 16 * 66 * 66 * 16
+    # zero-bordered slabs: (C/8) groups x (H+2) x (W+2) positions x 16 bytes; one image
+    # (32 tiles) splits its 16 groups 4 ways, with FP32 partial sums [4][64][4096] after the slabs
+    assert lib.dcn_forward_f16_workspace_bytes(ctypes.byref(jasna)) == 16 * 66 * 66 * 16 + 4 * 64 * 4096 * 4
+    two = DeformConvShape.jasna_propagation(2).to_c()    # 64 tiles: split 2 ways
+    assert lib.dcn_forward_f16_workspace_bytes(ctypes.byref(two)) == 2 * 16 * 66 * 66 * 16 + 2 * 2 * 64 * 4096 * 4
+    five = DeformConvShape.jasna_propagation(5).to_c()   # 160 tiles fill the GPU: no split
+    assert lib.dcn_forward_f16_workspace_bytes(ctypes.byref(five)) == 5 * 16 * 66 * 66 * 16
     # a 270x480 frame does not fit a shared-memory slab: global-gather kernel, corner pairs
     frame = DeformConvShape.jasna_propagation(1, 270, 480).to_c()
     assert lib.dcn_forward_f16_path(ctypes.byref(frame)) == _native.DCN_PATH_FUSED_TC
@@ -106,6 +111,18 @@ def test_kernel_choice_can_be_pinned_per_process():
     env = dict(os.environ, DCN_B200_FUSED_KERNEL="pairs", PYTHONPATH=str(REPO))
     out = subprocess.run([sys.executable, "-c", code], env=env, capture_output=True, text=True, check=True).stdout
     assert out.split() == [str(_native.DCN_PATH_FUSED_TC), str(18 * 8192)]
+
+
+def test_group_split_can_be_turned_off_per_process():
+    import os
+    import sys
+
+    code = ("import ctypes; from jasnamacos_b200 import _native; from jasnamacos_b200.deform_conv import "
+            "DeformConvShape as S; lib=_native.load(); s=S.jasna_propagation().to_c(); "
+            "print(lib.dcn_forward_f16_workspace_bytes(ctypes.byref(s)))")
+    env = dict(os.environ, DCN_B200_GROUP_SPLIT="0", PYTHONPATH=str(REPO))
+    out = subprocess.run([sys.executable, "-c", code], env=env, capture_output=True, text=True, check=True).stdout
+    assert int(out) == 16 * 66 * 66 * 16  # slabs only: no partial sums
 
 
 def test_null_pointers_are_rejected_before_any_device_work(lib):

@@ -154,8 +154,9 @@ def test_f16_config2_sampled_tiles(cuda_op, host_threads):
 
 
 def test_f16_config2_full_batch_properties(cuda_op):
-    """Full N=128 batch: per-tile independence (tile t of the batch == tile t run alone,
-    bit for bit), run-to-run determinism, finite outputs, and oracle parity on two tiles."""
+    """Full N=128 batch: per-tile independence (tiles t..t+4 of the batch == the same five
+    tiles run alone, bit for bit; five tiles are 160 128-pixel tiles, enough that the batch is
+    not group-split), run-to-run determinism, finite outputs, and oracle parity on two tiles."""
     import torch
 
     shape = synthetic.config_shape(2)
@@ -170,12 +171,14 @@ def test_f16_config2_full_batch_properties(cuda_op):
     assert torch.equal(out1, out2)
     assert int(flag.item()) == 0
     one = shape.with_batch(1)
+    five = shape.with_batch(5)
     per_in, per_off, per_msk, per_out = one.input_count, one.offset_count, one.mask_count, one.output_count
-    for t in (0, 63, 127):
-        single = cuda_op.forward_f16(one, x[t * per_in:(t + 1) * per_in], off[t * per_off:(t + 1) * per_off],
-                                     msk[t * per_msk:(t + 1) * per_msk], packed, b16)
+    assert cuda_op.workspace_bytes(five) == 5 * 16 * 66 * 66 * 16  # slabs only: no group split
+    for t in (0, 63, 123):
+        alone = cuda_op.forward_f16(five, x[t * per_in:(t + 5) * per_in], off[t * per_off:(t + 5) * per_off],
+                                    msk[t * per_msk:(t + 5) * per_msk], packed, b16)
         torch.cuda.synchronize()
-        assert torch.equal(single, out1[t * per_out:(t + 1) * per_out])
+        assert torch.equal(alone, out1[t * per_out:(t + 5) * per_out])
     for t in (5, 120):
         xs = x[t * per_in:(t + 1) * per_in].float().cpu().numpy()
         os_ = off[t * per_off:(t + 1) * per_off].float().cpu().numpy()
