@@ -52,7 +52,7 @@ constexpr int kChunks = 10;          // 9 taps + 1 zero chunk -> K = 80 = 5 MMAs
 constexpr int kMmasPerStage = kChunks / 2;
 constexpr int kBBlockBytes = BN * 32;                     // one K=16 block, SW32 K-major: 64 rows x 32 B
 constexpr int kBGroupBytes = kMmasPerStage * kBBlockBytes;  // 10 KB per deformable group
-constexpr int kStages = 4;                                // (tile, group) stages in flight
+constexpr int kStages = 6;                                // (tile, group) stages in flight
 constexpr int kOffRows = 2 * kTaps;                       // 18 offset rows per (tile, group)
 constexpr int kMaskRows = kTaps;                          // 9 mask rows
 constexpr uint32_t kStageTxBytes = (kOffRows + kMaskRows) * BM * 2;
@@ -64,7 +64,8 @@ constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kACol0 = kMaxTilesPerUnit * BN;  // 256: A stages after the accumulators
 constexpr uint32_t kAStageCols = kChunks * 4;       // 40 columns per stage
 constexpr uint32_t kIdleBackoffNs = 200;
-constexpr int kMaxSlabBytes = 87 * 1024;            // two slabs + ~51 KB of fixed buffers fit 227 KB
+constexpr int kMaxSlabBytes = 80 * 1024;            // two slabs + ~66 KB of fixed buffers fit 227 KB
+static_assert(kACol0 + kStages * kAStageCols <= kTmemCols, "accumulators and A stages exceed TMEM");
 
 // Shared memory: fixed part; the two slabs follow it (size depends on H, W).
 struct __align__(1024) Smem {
