@@ -7,13 +7,15 @@
 //    happens and the result is bit-identical to the CPU reference.
 //  * FP16 storage / FP32 math: replaces deform_conv2d_fp16 (MetalShader.swift:126-174).
 //
-// Work split (not the reference's one-thread-per-output): a block owns 32
-// consecutive output pixels and up to 64 output channels of one convolution
-// group.  For a chunk of input channels it first evaluates every
-// sampled*mask product once into shared memory (coalesced offset/mask reads,
-// one bilinear sample per (ic, tap, pixel)), then 8 warps accumulate 8 output
-// channels each from shared memory.  Per output the additions still run in the
-// reference order (bias, then ic, ky, kx), which is all bit-exactness needs.
+// Work split (not the reference's one-thread-per-output): a block owns 16
+// consecutive output pixels and up to 64 output channels of one convolution group;
+// thread (pixel p, channel quad g) accumulates channels 4g..4g+3 of pixel p.  The
+// reduction index k = ic * KA + tap runs in chunks of 64: per chunk the block
+// evaluates every sampled*mask product of its 16 pixels once into shared memory
+// (four independent samples per thread, their loads in flight together) and stages
+// the chunk's weights there, transposed to [k][oc].  Per output the additions still
+// run in the reference order (bias, then ic, ky, kx), which is all bit-exactness
+// needs.
 #include <cuda_fp16.h>
 
 #include "dcn_common.cuh"
@@ -22,10 +24,12 @@ namespace dcn {
 
 namespace {
 
-constexpr int kPix = 32;        // output pixels per block (one per lane)
-constexpr int kOcLanes = 8;     // warps per block; each accumulates 8 channels
-constexpr int kOcPerBlock = 64; // output channels per block (8 per thread)
-constexpr int kThreads = kPix * kOcLanes;
+constexpr int kPix = 16;        // output pixels per block
+constexpr int kOcPerBlock = 64; // output channels per block
+constexpr int kQuads = kOcPerBlock / 4;
+constexpr int kThreads = kPix * kQuads;  // 256
+constexpr int kChunk = 64;      // reduction steps (ic, tap) per shared-memory chunk
+constexpr int kSamplesPerThread = kChunk * kPix / kThreads;  // 4
 
 __device__ __forceinline__ float load_val(const float *p, int64_t i) { return p[i]; }
 __device__ __forceinline__ float load_val(const __half *p, int64_t i) { return __half2float(p[i]); }
@@ -57,126 +61,139 @@ __device__ __forceinline__ float sample_exact(const T *plane, int H, int W, floa
     return __fadd_rn(__fadd_rn(__fadd_rn(t0, t1), t2), t3);
 }
 
-// grid.x: ceil(N*out_plane / 32) pixel blocks; grid.y: G * ceil(opg / 64).
-// Dynamic shared memory: chunk_ic * KA * 32 floats.
+// Shared-memory weight chunk [k][oc] with the 4-channel quads of row k XOR-swizzled by
+// k mod 16, so the transposing stores (consecutive k from consecutive threads) spread
+// over the banks while a quad stays one aligned 16-byte load.
+__device__ __forceinline__ int wslot(int k, int oc) { return k * kOcPerBlock + (((oc >> 2) ^ (k & 15)) << 2) + (oc & 3); }
+
+// grid.x: ceil(N*out_plane / 16) pixel blocks; grid.y: G * ceil(opg / 64).
 template <typename T>
 __global__ void __launch_bounds__(kThreads)
     direct_kernel(Params p, const SplitInput<T> input, const T *__restrict__ offset,
                   const T *__restrict__ mask, const T *__restrict__ weight,
-                  const T *__restrict__ bias, T *__restrict__ output, int chunk_ic) {
-    extern __shared__ float s_samples[];  // [chunk_ic][KA][kPix]
+                  const T *__restrict__ bias, T *__restrict__ output) {
+    __shared__ float s_samples[kChunk][kPix];
+    __shared__ __align__(16) float s_w[kChunk * kOcPerBlock];
     const int tid = threadIdx.x;
-    const int lane = tid % kPix;
-    const int oc_lane = tid / kPix;
+    const int px_lane = tid % kPix;
+    const int quad = tid / kPix;
     const int oc_blocks = (p.opg + kOcPerBlock - 1) / kOcPerBlock;
     const int group = blockIdx.y / oc_blocks;
     const int oc_block = blockIdx.y % oc_blocks;
+    const int oc_base = oc_block * kOcPerBlock;                 // first channel of the block, within the group
+    const int oc_count = min(kOcPerBlock, p.opg - oc_base);
     const int64_t total_pix = static_cast<int64_t>(p.N) * p.out_plane;
     const int64_t pix0 = static_cast<int64_t>(blockIdx.x) * kPix;
+    const int K = p.cpg * p.KA;                                 // reduction length per output
 
-    // The pixel this thread accumulates (and, in phase 1, samples for).
-    const int64_t my_pix = pix0 + lane;
+    // The pixel this thread accumulates -- and samples: in phase 1 thread (p, q) evaluates
+    // reduction steps 4q .. 4q+3 of the chunk for pixel p.
+    const int64_t my_pix = pix0 + px_lane;
     const bool my_valid = my_pix < total_pix;
     const int my_n = my_valid ? static_cast<int>(my_pix / p.out_plane) : 0;
     const int my_spatial = my_valid ? static_cast<int>(my_pix % p.out_plane) : 0;
+    const int my_oy = my_spatial / p.WO;
+    const int my_ox = my_spatial - my_oy * p.WO;
+    const int base_y = my_oy * p.SH - p.PH;
+    const int base_x = my_ox * p.SW - p.PW;
+    const T *off_px = offset + static_cast<int64_t>(my_n) * 2 * p.OG * p.KA * p.out_plane + my_spatial;
+    const T *msk_px = mask + static_cast<int64_t>(my_n) * p.OG * p.KA * p.out_plane + my_spatial;
 
-    float acc[8];
+    float acc[4];
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
-        const int oc_local = oc_block * kOcPerBlock + oc_lane + kOcLanes * j;
+    for (int j = 0; j < 4; ++j) {
+        const int oc_local = oc_base + quad * 4 + j;
         acc[j] = oc_local < p.opg ? load_val(bias, group * p.opg + oc_local) : 0.0f;
     }
 
-    const int per_ic = p.KA * kPix;
-    for (int ic0 = 0; ic0 < p.cpg; ic0 += chunk_ic) {
-        const int nic = min(chunk_ic, p.cpg - ic0);
-        // Phase 1: sampled * mask for (ic, tap, pixel) of this chunk.
-        for (int e = tid; e < nic * per_ic; e += kThreads) {
-            const int lic = e / per_ic;
-            const int k = (e / kPix) % p.KA;
-            const int px = e % kPix;  // == lane for every e handled by this thread
-            const int64_t pix = pix0 + px;
-            float v = 0.0f;
-            if (pix < total_pix) {
-                const int n = static_cast<int>(pix / p.out_plane);
-                const int spatial = static_cast<int>(pix % p.out_plane);
-                const int oy = spatial / p.WO;
-                const int ox = spatial % p.WO;
-                const int ic = group * p.cpg + ic0 + lic;
-                const int og = ic / p.cpog;
-                const int ky = k / p.KW;
-                const int kx = k % p.KW;
-                const int offset_channel = 2 * (og * p.KA + k);
-                const int64_t obase = static_cast<int64_t>(n) * 2 * p.OG * p.KA * p.out_plane;
-                const float off_y = load_val(offset, obase + static_cast<int64_t>(offset_channel) * p.out_plane + spatial);
-                const float off_x = load_val(offset, obase + static_cast<int64_t>(offset_channel + 1) * p.out_plane + spatial);
-                const float y = __fadd_rn(static_cast<float>(oy * p.SH - p.PH + ky * p.DH), off_y);
-                const float x = __fadd_rn(static_cast<float>(ox * p.SW - p.PW + kx * p.DW), off_x);
-                const T *plane = input.channel(n, ic, p.in_plane);
-                const float sampled = sample_exact(plane, p.H, p.W, y, x);
-                const int64_t mbase = static_cast<int64_t>(n) * p.OG * p.KA * p.out_plane;
-                const float m = load_val(mask, mbase + static_cast<int64_t>(og * p.KA + k) * p.out_plane + spatial);
-                v = __fmul_rn(sampled, m);
-            }
-            s_samples[e] = v;
-        }
-        __syncthreads();
-        // Phase 2: acc += (sampled * mask) * weight in the order ic, ky, kx.
-        if (my_valid) {
-            for (int lic = 0; lic < nic; ++lic) {
-                for (int k = 0; k < p.KA; ++k) {
-                    const float sv = s_samples[(lic * p.KA + k) * kPix + lane];
+    for (int k0 = 0; k0 < K; k0 += kChunk) {
+        const int nk = min(kChunk, K - k0);
+        // Phase 1: sampled * mask for this thread's four consecutive steps (ic, tap).
+        float sv[kSamplesPerThread];
+        {
+            const int kg0 = k0 + quad * kSamplesPerThread;
+            int lic = kg0 / p.KA;
+            int tap = kg0 - lic * p.KA;
+            int ky = tap / p.KW;
+            int kx = tap - ky * p.KW;
 #pragma unroll
-                    for (int j = 0; j < 8; ++j) {
-                        const int oc_local = oc_block * kOcPerBlock + oc_lane + kOcLanes * j;
-                        if (oc_local < p.opg) {
-                            const int oc = group * p.opg + oc_local;
-                            const float w = load_val(
-                                weight, (static_cast<int64_t>(oc) * p.cpg + ic0 + lic) * p.KA + k);
-                            acc[j] = __fadd_rn(acc[j], __fmul_rn(sv, w));
-                        }
-                    }
+            for (int j = 0; j < kSamplesPerThread; ++j) {
+                float v = 0.0f;
+                if (quad * kSamplesPerThread + j < nk && my_valid) {
+                    const int ic = group * p.cpg + lic;
+                    const int og = ic / p.cpog;
+                    const int pair = og * p.KA + tap;
+                    const float off_y = load_val(off_px, static_cast<int64_t>(2 * pair) * p.out_plane);
+                    const float off_x = load_val(off_px, static_cast<int64_t>(2 * pair + 1) * p.out_plane);
+                    const float y = __fadd_rn(static_cast<float>(base_y + ky * p.DH), off_y);
+                    const float x = __fadd_rn(static_cast<float>(base_x + kx * p.DW), off_x);
+                    const float sampled = sample_exact(input.channel(my_n, ic, p.in_plane), p.H, p.W, y, x);
+                    const float m = load_val(msk_px, static_cast<int64_t>(pair) * p.out_plane);
+                    v = __fmul_rn(sampled, m);
+                }
+                sv[j] = v;
+                // next step: tap + 1, carrying into kx, ky and the channel
+                if (++kx == p.KW) {
+                    kx = 0;
+                    ++ky;
+                }
+                if (++tap == p.KA) {
+                    tap = 0;
+                    ky = 0;
+                    kx = 0;
+                    ++lic;
                 }
             }
+        }
+        // Weights of the chunk, [k][oc] (consecutive threads take consecutive k of one
+        // channel, so the global reads follow OIHW).
+        float wv[kChunk * kOcPerBlock / kThreads];
+#pragma unroll
+        for (int i = 0; i < kChunk * kOcPerBlock / kThreads; ++i) {
+            const int e = tid + i * kThreads;
+            const int kl = e % kChunk;
+            const int ol = e / kChunk;
+            wv[i] = (kl < nk && ol < oc_count)
+                        ? load_val(weight, static_cast<int64_t>(group * p.opg + oc_base + ol) * K + k0 + kl)
+                        : 0.0f;
+        }
+#pragma unroll
+        for (int i = 0; i < kChunk * kOcPerBlock / kThreads; ++i) {
+            const int e = tid + i * kThreads;
+            s_w[wslot(e % kChunk, e / kChunk)] = wv[i];
+        }
+#pragma unroll
+        for (int j = 0; j < kSamplesPerThread; ++j) s_samples[quad * kSamplesPerThread + j][px_lane] = sv[j];
+        __syncthreads();
+        // Phase 2: acc += (sampled * mask) * weight in the order ic, ky, kx.
+        for (int kl = 0; kl < nk; ++kl) {
+            const float v = s_samples[kl][px_lane];
+            const float4 w = *reinterpret_cast<const float4 *>(&s_w[wslot(kl, quad * 4)]);
+            acc[0] = __fadd_rn(acc[0], __fmul_rn(v, w.x));
+            acc[1] = __fadd_rn(acc[1], __fmul_rn(v, w.y));
+            acc[2] = __fadd_rn(acc[2], __fmul_rn(v, w.z));
+            acc[3] = __fadd_rn(acc[3], __fmul_rn(v, w.w));
         }
         __syncthreads();
     }
 
     if (my_valid) {
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-            const int oc_local = oc_block * kOcPerBlock + oc_lane + kOcLanes * j;
-            if (oc_local < p.opg) {
-                const int oc = group * p.opg + oc_local;
-                store_val(output, output_index(p, my_n, oc, my_spatial), acc[j]);
-            }
+        for (int j = 0; j < 4; ++j) {
+            const int oc_local = oc_base + quad * 4 + j;
+            if (oc_local < p.opg)
+                store_val(output, output_index(p, my_n, group * p.opg + oc_local, my_spatial), acc[j]);
         }
     }
-}
-
-// Input channels per shared-memory chunk: keep chunk * KA * 32 floats <= 32 KiB
-// (but at least one channel, for kernels up to 1024 taps = 128 KiB).
-int chunk_channels(const Params &p) {
-    int c = 256 / p.KA;
-    if (c < 1) c = 1;
-    if (c > p.cpg) c = p.cpg;
-    return c;
 }
 
 template <typename T>
 cudaError_t launch_direct(const Params &p, const SplitInput<T> &input, const T *offset, const T *mask,
                           const T *weight, const T *bias, T *output, cudaStream_t stream) {
-    const int chunk = chunk_channels(p);
-    const size_t smem = static_cast<size_t>(chunk) * p.KA * kPix * sizeof(float);
-    if (smem > 48 * 1024) {
-        cudaError_t e = cudaFuncSetAttribute(direct_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             static_cast<int>(smem));
-        if (e != cudaSuccess) return e;
-    }
     const int64_t total_pix = static_cast<int64_t>(p.N) * p.out_plane;
     const int oc_blocks = (p.opg + kOcPerBlock - 1) / kOcPerBlock;
     dim3 grid(static_cast<unsigned>((total_pix + kPix - 1) / kPix), static_cast<unsigned>(p.G * oc_blocks));
-    direct_kernel<T><<<grid, kThreads, smem, stream>>>(p, input, offset, mask, weight, bias, output, chunk);
+    direct_kernel<T><<<grid, kThreads, 0, stream>>>(p, input, offset, mask, weight, bias, output);
     return cudaGetLastError();
 }
 
