@@ -113,7 +113,7 @@ typedef enum dcn_path {
     DCN_PATH_FUSED_TC = 1,    /* sm_100a fused gather + tcgen05 implicit GEMM, gathers from
                                  global memory (any image size) */
     DCN_PATH_SLAB_TC = 2      /* the same operator with each deformable group's input staged
-                                 whole in shared memory (3x3 kernels, images up to ~70x70) */
+                                 whole in shared memory (3x3 kernels, images up to ~69x69) */
 } dcn_path;
 
 /* ---- status / shape helpers ------------------------------------------------ */
