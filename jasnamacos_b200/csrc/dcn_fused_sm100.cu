@@ -9,8 +9,10 @@
 // the SM: producer warps bilinearly sample, mask and round each 8-channel
 // chunk to FP16 and write it into tensor memory, where tcgen05.mma consumes it
 // as the A operand (M = 128 output pixels, N = 64 output channels, K = 16 per
-// instruction) against weights that stay resident in shared memory for the
-// whole persistent kernel.
+// instruction) against the weights, streamed from L2 one 8 KB K-block per stage.
+// Keeping shared memory small matters here: the gathers read global memory through
+// L1, which shares the SM's 256 KB with shared memory (holding all 144 KB of weights
+// resident left about 60 KB of L1; streaming them leaves about 190 KB).
 //
 // GEMM view of one output tile (128 consecutive pixels of one image):
 //   out[p][oc] = bias[oc] + sum_kk A[p][kk] * B[kk][oc]
@@ -19,8 +21,8 @@
 // One "stage" = 8 chunks = 64 K-elements = 4 MMAs.
 //
 // Warp roles (14 warps, one CTA per SM, persistent over tiles):
-//   warp 0      loader   : weights once (bulk copy), then per stage the
-//                          16 offset + 8 mask channel rows of the tile (TMA 3D)
+//   warp 0      loader   : per stage the 16 offset + 8 mask channel rows of the
+//                          tile (TMA 3D) and the stage's 8 KB weight K-block (bulk copy)
 //   warp 1      MMA      : TMEM allocation; one thread issues tcgen05.mma
 //   warps 2-5   epilogue : TMEM -> registers, +bias, FP16, NCHW stores, Inf/NaN flag
 //   warps 6-13  producers: gather + bilinear + mask -> tcgen05.st into the A stage
@@ -45,7 +47,7 @@ constexpr int BM = 128;                 // output pixels per tile (TMEM lanes)
 constexpr int BN = 64;                  // output channels
 constexpr int kChunksPerStage = 8;      // 8 x 8 channels = 64 K-elements
 constexpr int kStages = 4;              // A (TMEM) and offset/mask (smem) ring depth
-constexpr int kMaxKBlocks = 18;         // resident weight K-blocks (18 x 64 = 1152)
+constexpr int kMaxKBlocks = 18;         // K-blocks per tile (18 x 64 = 1152): the chunk table size
 constexpr int kBBlockBytes = BN * 128;  // one 64-wide K-block of B: 64 rows x 128 B
 constexpr int kThreads = 16 * 32;  // 4 warpgroups: control (loader, MMA), epilogue, 2 x producers
 constexpr uint32_t kIdleBackoffNs = 200;
@@ -60,7 +62,7 @@ constexpr uint32_t kACol0 = 2 * BN;
 constexpr uint32_t kAStageCols = kChunksPerStage * 4;  // 8 chunks x 16 B = 32 columns
 
 struct __align__(1024) Smem {
-    uint8_t b[kMaxKBlocks][kBBlockBytes];  // weights, 128B-swizzled K-major (1024-aligned)
+    uint8_t b[kStages][kBBlockBytes];      // the stages' weight K-blocks, 128B-swizzled K-major (1024-aligned)
     __half off[kStages][kOffRows][BM];     // offset rows of the stage (TMA box)
     __half msk[kStages][kMaskRows][BM];    // mask rows of the stage (TMA box)
     float bias[BN];
@@ -71,7 +73,6 @@ struct __align__(1024) Smem {
     uint64_t a_empty[kStages];   // MMAs reading the A stage completed
     uint64_t acc_full[2];        // accumulator buffer complete
     uint64_t acc_empty[2];       // epilogue drained the accumulator buffer
-    uint64_t w_full;             // weights resident
     uint32_t tmem_base;
     int abort_flag;
 };
@@ -132,7 +133,6 @@ __global__ void __launch_bounds__(kThreads, 1)
             mbar_init(&s.acc_full[i], 1);
             mbar_init(&s.acc_empty[i], kEpilogueWarps);
         }
-        mbar_init(&s.w_full, 1);
         s.abort_flag = 0;
         fence_mbarrier_init();
     }
@@ -164,9 +164,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (wg == 0) {
         if (warp == 0 && lane == 0) {
             // ------------------------------------------------------------ loader
-            mbar_arrive_expect_tx(&s.w_full, static_cast<uint32_t>(a.kb) * kBBlockBytes);
-            for (int b = 0; b < a.kb; ++b)
-                bulk_copy_g2s(s.b[b], a.packed_w + static_cast<size_t>(b) * kBBlockBytes, kBBlockBytes, &s.w_full);
             uint32_t it = 0;
             bool ok = true;
             for (int tile = blockIdx.x; tile < a.num_tiles && ok; tile += gridDim.x) {
@@ -175,18 +172,22 @@ __global__ void __launch_bounds__(kThreads, 1)
                 for (int sb = 0; sb < a.kb; ++sb, ++it) {
                     const uint32_t st = it % kStages;
                     const uint32_t ph = (it / kStages) & 1u;
-                    if (!mbar_wait_bounded(&s.om_empty[st], ph ^ 1u, abort_flag)) {
+                    // The stage's offset/mask rows are free once the producers read them, its
+                    // weight block once the MMAs of its previous use completed.
+                    if (!mbar_wait_bounded(&s.om_empty[st], ph ^ 1u, abort_flag) ||
+                        !mbar_wait_bounded(&s.a_empty[st], ph ^ 1u, abort_flag)) {
                         signal_abort(s, a.err);
                         ok = false;
                         break;
                     }
-                    mbar_arrive_expect_tx(&s.om_full[st], kStageTxBytes);
+                    mbar_arrive_expect_tx(&s.om_full[st], kStageTxBytes + kBBlockBytes);
                     tma_load_3d(&s.off[st][0][0], &tmap_off, &s.om_full[st], px0, kOffRows * sb, n);
                     tma_load_3d(&s.msk[st][0][0], &tmap_msk, &s.om_full[st], px0, kMaskRows * sb, n);
+                    bulk_copy_g2s(s.b[st], a.packed_w + static_cast<size_t>(sb) * kBBlockBytes, kBBlockBytes,
+                                  &s.om_full[st]);
                 }
             }
             // Drain: wait until every copy this thread issued has landed.
-            mbar_wait_bounded(&s.w_full, 0, nullptr);
             for (uint32_t k = 0; k < kStages && k < it; ++k) {
                 const uint32_t last = it - 1 - k;
                 mbar_wait_bounded(&s.om_full[last % kStages], (last / kStages) & 1u, nullptr);
@@ -194,10 +195,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         } else if (warp == 1 && lane == 0) {
             // --------------------------------------------------------------- MMA
             const uint32_t idesc = make_idesc_f16_f32(BM, BN);
-            const uint32_t b_base = smem_addr(&s.b[0][0]);
-            bool ok = mbar_wait_bounded(&s.w_full, 0, abort_flag);
-            if (!ok) signal_abort(s, a.err);
-            tc_fence_after();
+            bool ok = true;
             uint32_t it = 0;
             uint32_t tcount = 0;
             uint64_t *last_bar = nullptr;
@@ -215,17 +213,21 @@ __global__ void __launch_bounds__(kThreads, 1)
                 for (int sb = 0; sb < a.kb; ++sb, ++it) {
                     const uint32_t st = it % kStages;
                     const uint32_t ph = (it / kStages) & 1u;
-                    if (!mbar_wait_bounded(&s.a_full[st], ph, abort_flag)) {
+                    // a_full: the producers stored the A stage; om_full: the stage's weight
+                    // block landed (already true by then: the producers waited for it).
+                    if (!mbar_wait_bounded(&s.a_full[st], ph, abort_flag) ||
+                        !mbar_wait_bounded(&s.om_full[st], ph, abort_flag)) {
                         signal_abort(s, a.err);
                         ok = false;
                         break;
                     }
                     tc_fence_after();
                     const uint32_t a_tmem = tmem + kACol0 + st * kAStageCols;
+                    const uint32_t b_base = smem_addr(&s.b[st][0]);
 #pragma unroll
                     for (int kk = 0; kk < 4; ++kk) {
                         // K = 16 FP16 per MMA: 8 TMEM columns of A, 32 bytes along a swizzled B row.
-                        const uint64_t bdesc = make_sw128_kmajor_desc(b_base + sb * kBBlockBytes + kk * 32);
+                        const uint64_t bdesc = make_sw128_kmajor_desc(b_base + kk * 32);
                         umma_f16_ts(d_tmem, a_tmem + kk * 8, bdesc, idesc, (sb | kk) != 0 ? 1u : 0u);
                     }
                     umma_commit(&s.a_empty[st]);

@@ -24,12 +24,15 @@ def _p(t):
     return ctypes.c_void_p(t.data_ptr())
 
 
-def test_static_scratch_matches_workspace_entry_point_twice():
+@pytest.mark.parametrize("batch", [4, 1], ids=["4_tiles", "1_tile_group_split"])
+def test_static_scratch_matches_workspace_entry_point_twice(batch):
+    """Four 64x64 tiles (slabs only) and one tile, whose 16 deformable groups are split across
+    SMs with their FP32 partial sums kept in the static scratch too."""
     import torch
 
     assert torch.cuda.is_available()
     lib = _native.load()
-    shape = DeformConvShape.jasna_propagation(batch=4)  # at most 4 x 2.03 MiB of scratch, under 16 MiB
+    shape = DeformConvShape.jasna_propagation(batch=batch)
     c_shape = shape.to_c()
     assert lib.dcn_static_scratch_bytes() == 16 << 20
     w, b = synthetic.weights(shape, 21)
@@ -39,6 +42,7 @@ def test_static_scratch_matches_workspace_entry_point_twice():
     assert lib.dcn_prepack_weights(ctypes.byref(c_shape), _p(w16), _native.DCN_DTYPE_F16, _native.DCN_WEIGHT_OIHW,
                                    _p(packed), None) == _native.DCN_OK
     ws_bytes = lib.dcn_forward_f16_workspace_bytes(ctypes.byref(c_shape))
+    assert ws_bytes <= lib.dcn_static_scratch_bytes()
     ws = torch.empty(ws_bytes, dtype=torch.uint8, device="cuda")
 
     for call, seed in enumerate((31, 32)):  # two calls in a row, different inputs
