@@ -459,7 +459,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                                                                  __half2float(s.flow[st][1][r])));
                             off_x = __half2float(__float2half_rn(10.0f * tanh_approx(off_x) +
                                                                  __half2float(s.flow[st][0][r])));
-                            mk = __half2float(__float2half_rn(__frcp_rn(1.0f + __expf(-mk))));
+                            mk = __half2float(__float2half_rn(__fdividef(1.0f, 1.0f + __expf(-mk))));
                         }
                         const float y = (bfy[t] + tyf[i]) + off_y;
                         const float x = (bfx[t] + txf[i]) + off_x;
