@@ -374,7 +374,12 @@ def run_ours(args):
                                   args.steps) / args.steps
         regroup_ms = event_time_ms(graphed(lambda: op.regroup_input(shape, x, workspace=ws), use_graph),
                                    args.steps) / args.steps
-        launches_per_step = 2
+        # pre-pass + tensor-core kernel, + the reduction pass when the slab kernel splits the
+        # deformable groups (batches with fewer 128-pixel tiles than SMs: the workspace then
+        # holds FP32 partial sums past the zero-bordered slabs)
+        slabs = shape.batch * shape.offset_groups * (shape.input_height + 2) * (shape.input_width + 2) * 16
+        split = path == _native.DCN_PATH_SLAB_TC and op.workspace_bytes(shape) > (slabs + 255) // 256 * 256
+        launches_per_step = 3 if split else 2
     else:
         kernel_ms = ms / args.steps
         launches_per_step = 1 if cfg["f32"] else 2
@@ -483,7 +488,8 @@ def run_ours(args):
                               "setting for this config)"),
                        "parallelism": (f"tile shards x{world}, no data-path collective" if cfg["sharded"] else
                                        f"{world} independent replicas"),
-                       "launch": "CUDA graph replay per step" if use_graph else "direct launches per step"},
+                       "launch": "CUDA graph replay per step" if use_graph else "direct launches per step",
+                       "kernels_per_step": launches_per_step},
             "roofline": {"bound": "hbm", "achieved": achieved_gbs, "peak": peaks["hbm_gbs"], "unit": "GB/s",
                          "frac": achieved_gbs / peaks["hbm_gbs"], "traffic": traffic,
                          "peak_source": f"{peak_kind} hbm_gbs", "kernel": kernel,
