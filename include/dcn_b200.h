@@ -225,10 +225,10 @@ dcn_status dcn_forward_f16_grouped(const dcn_shape *shape, void *input_grouped,
  * offset residues, then G*KH*KW mask logits; 432 channels for Jasna), flow1/flow2 are
  * [N][2][Ho][Wo] FP16 in (x, y) order.  offset = FP16(10*tanh(residue) + flow) with dy
  * channels taking the flow's y row and deformable groups [0, G/2) flow1, the rest flow2;
- * mask = FP16(sigmoid(logit)).  On the slab path the transform runs inside the
- * convolution and the offset/mask tensors never exist in memory; other tensor-core
- * shapes run the offset producer into the workspace first.  Requires an even G and a
- * tensor-core path (else DCN_ERR_UNSUPPORTED); raw and flows 16-byte aligned. */
+ * mask = FP16(sigmoid(logit)).  On both tensor-core paths the transform runs inside the
+ * convolution's producers and the offset/mask tensors never exist in memory; the
+ * workspace is the one dcn_forward_f16 takes.  Requires an even G and a tensor-core path
+ * (else DCN_ERR_UNSUPPORTED); raw and flows 16-byte aligned. */
 size_t dcn_forward_f16_raw_workspace_bytes(const dcn_shape *shape);
 dcn_status dcn_forward_f16_raw(const dcn_shape *shape, const void *input, const void *raw,
                                const void *flow1, const void *flow2, const void *packed_weight,

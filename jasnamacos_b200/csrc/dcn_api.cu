@@ -44,6 +44,10 @@ cudaError_t launch_regroup_c8(const Params &p, const SplitInput<__half> &input, 
 cudaError_t launch_fused_grouped(const Params &p, const void *input_c8, const __half *offset, const __half *mask,
                                  const uint8_t *packed_w, const __half *bias, __half *output, uint32_t *flag,
                                  int sm_count, uint32_t *err, cudaStream_t stream);
+cudaError_t launch_fused_grouped_raw(const Params &p, const void *input_c8, const __half *raw,
+                                     const __half *flow1, const __half *flow2, const uint8_t *packed_w,
+                                     const __half *bias, __half *output, uint32_t *flag, int sm_count,
+                                     uint32_t *err, cudaStream_t stream);
 bool slab_supported(const Params &p);
 size_t slab_workspace_bytes(const Params &p);
 size_t slab_packed_weight_bytes(const Params &p);
@@ -459,23 +463,15 @@ dcn_status dcn_prepare_offsets_f16(int64_t plane, const void *raw, const void *f
                                             reinterpret_cast<cudaStream_t>(stream)));
 }
 
-namespace {
-
-size_t round256(size_t v) { return (v + 255) & ~size_t{255}; }
-
-// Bytes of the FP16 offset and mask tensors of a shape (the two-step form of the raw entry point).
-size_t offset_bytes(const Params &p) { return round256(static_cast<size_t>(p.N) * 2 * p.OG * p.KA * p.out_plane * 2); }
-size_t mask_bytes(const Params &p) { return round256(static_cast<size_t>(p.N) * p.OG * p.KA * p.out_plane * 2); }
-
-}  // namespace
-
+// Both tensor-core kernels make the offsets and masks inside their producers, so the raw
+// form needs the same workspace as dcn_forward_f16 (the regrouped input, plus the partial
+// sums of a group-split slab batch).
 size_t dcn_forward_f16_raw_workspace_bytes(const dcn_shape *shape) {
     if (validate(shape) != DCN_OK) return 0;
     const Params p = make_params(*shape);
     const dcn_path path = select_path(p);
     if (path == DCN_PATH_DIRECT || p.OG % 2 != 0) return 0;
-    const size_t base = round256(dcn_forward_f16_workspace_bytes(shape));
-    return path == DCN_PATH_SLAB_TC ? base : base + offset_bytes(p) + mask_bytes(p);
+    return dcn_forward_f16_workspace_bytes(shape);
 }
 
 dcn_status dcn_forward_f16_raw_io(const dcn_shape *shape, const dcn_io *io, const void *input, const void *raw,
@@ -504,18 +500,14 @@ dcn_status dcn_forward_f16_raw_io(const dcn_shape *shape, const dcn_io *io, cons
     const auto *f2 = static_cast<const __half *>(flow2);
     cudaError_t e = launch_regroup(path, p, in, workspace, s);
     if (e != cudaSuccess) return from_cuda(e);
+    const auto *w = static_cast<const uint8_t *>(packed_weight);
+    const auto *b = static_cast<const __half *>(bias);
+    auto *out = static_cast<__half *>(output);
     if (path == DCN_PATH_SLAB_TC)
-        return from_cuda(launch_slab_grouped_raw(p, workspace, r, f1, f2, static_cast<const uint8_t *>(packed_weight),
-                                                 static_cast<const __half *>(bias), static_cast<__half *>(output),
-                                                 nonfinite_flag, dev->sm_count, dev->err_word, s));
-    // Two steps for the global-gather kernel: the offset producer into the workspace, then the operator.
-    uint8_t *ws = static_cast<uint8_t *>(workspace);
-    const size_t base = round256(dcn_forward_f16_workspace_bytes(shape));
-    auto *offset = reinterpret_cast<__half *>(ws + base);
-    auto *mask = reinterpret_cast<__half *>(ws + base + offset_bytes(p));
-    e = launch_prepare_offsets(p.N, p.OG * p.KA, p.out_plane, r, f1, f2, offset, mask, s);
-    if (e != cudaSuccess) return from_cuda(e);
-    return launch_grouped(path, p, workspace, offset, mask, packed_weight, bias, output, nonfinite_flag, dev, s);
+        return from_cuda(launch_slab_grouped_raw(p, workspace, r, f1, f2, w, b, out, nonfinite_flag, dev->sm_count,
+                                                 dev->err_word, s));
+    return from_cuda(launch_fused_grouped_raw(p, workspace, r, f1, f2, w, b, out, nonfinite_flag, dev->sm_count,
+                                              dev->err_word, s));
 }
 
 dcn_status dcn_forward_f16_raw(const dcn_shape *shape, const void *input, const void *raw, const void *flow1,

@@ -28,29 +28,33 @@ __global__ void flag_non_finite_kernel(const __half *__restrict__ values, int64_
     if (__any_sync(0xffffffffu, bad) && (threadIdx.x % 32) == 0) atomicOr(flag, DCN_FLAG_NONFINITE);
 }
 
-// One thread per (image, channel, spatial) of the raw tensor [N][3*gka][plane]
-// (gka = deformable groups x taps; 144 for Jasna: 288 offset residues + 144 mask logits).
-// Offset channels [0, gka) take flow1, [gka, 2*gka) flow2.
-__global__ void prepare_offsets_kernel(int64_t n_images, int gka, int64_t plane, const __half *__restrict__ raw,
-                                       const __half *__restrict__ flow1, const __half *__restrict__ flow2,
-                                       __half *__restrict__ offset, __half *__restrict__ mask) {
-    const int64_t gid = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-    const int64_t per_image = 3 * static_cast<int64_t>(gka) * plane;
-    if (gid >= n_images * per_image) return;
-    const int64_t n = gid / per_image;
-    const int64_t rest = gid % per_image;
-    const int64_t channel = rest / plane;
-    const int64_t spatial = rest % plane;
-    const float v = __half2float(raw[gid]);
-    if (channel < 2 * gka) {
-        const int64_t local = channel % gka;
-        const __half *flow = (channel < gka ? flow1 : flow2) + n * 2 * plane;
-        // The flow is stored (x, y); offsets are interleaved (dy, dx), so even channels take row 1.
-        const int64_t flow_channel = (local & 1) == 0 ? 1 : 0;
-        const float residue = 10.0f * tanhf(v);
-        offset[n * 2 * gka * plane + rest] = __float2half_rn(residue + __half2float(flow[flow_channel * plane + spatial]));
-    } else {
-        mask[(n * gka + channel - 2 * gka) * plane + spatial] = __float2half_rn(1.0f / (1.0f + expf(-v)));
+// Raw tensor [N][3*gka][plane] (gka = deformable groups x taps; 144 for Jasna: 288 offset
+// residues + 144 mask logits).  Grid: x over the plane, y = raw channel, z strides over the
+// images (no 64-bit division per element).  Offset channels [0, gka) take flow1, [gka, 2*gka)
+// flow2.
+__global__ void __launch_bounds__(256) prepare_offsets_kernel(int64_t n_images, int gka, int64_t plane,
+                                                              const __half *__restrict__ raw,
+                                                              const __half *__restrict__ flow1,
+                                                              const __half *__restrict__ flow2,
+                                                              __half *__restrict__ offset,
+                                                              __half *__restrict__ mask) {
+    const int64_t spatial = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (spatial >= plane) return;
+    const int channel = blockIdx.y;
+    const int channels = 3 * gka;
+    for (int64_t n = blockIdx.z; n < n_images; n += gridDim.z) {
+        const float v = __half2float(raw[(n * channels + channel) * plane + spatial]);
+        if (channel < 2 * gka) {
+            const int local = channel % gka;
+            const __half *flow = (channel < gka ? flow1 : flow2) + n * 2 * plane;
+            // The flow is stored (x, y); offsets are interleaved (dy, dx), so even channels take row 1.
+            const int flow_channel = (local & 1) == 0 ? 1 : 0;
+            const float residue = 10.0f * tanhf(v);
+            offset[(n * 2 * gka + channel) * plane + spatial] =
+                __float2half_rn(residue + __half2float(flow[flow_channel * plane + spatial]));
+        } else {
+            mask[(n * gka + channel - 2 * gka) * plane + spatial] = __float2half_rn(1.0f / (1.0f + expf(-v)));
+        }
     }
 }
 
@@ -74,9 +78,10 @@ cudaError_t launch_flag_non_finite(const __half *values, int64_t count, uint32_t
 
 cudaError_t launch_prepare_offsets(int64_t n_images, int gka, int64_t plane, const __half *raw, const __half *flow1,
                                    const __half *flow2, __half *offset, __half *mask, cudaStream_t stream) {
-    const int64_t total = n_images * 3 * gka * plane;
-    prepare_offsets_kernel<<<static_cast<unsigned>((total + 255) / 256), 256, 0, stream>>>(
-        n_images, gka, plane, raw, flow1, flow2, offset, mask);
+    if (n_images <= 0 || plane <= 0) return cudaSuccess;
+    const dim3 grid(static_cast<unsigned>((plane + 255) / 256), static_cast<unsigned>(3 * gka),
+                    static_cast<unsigned>(n_images < 65535 ? n_images : 65535));
+    prepare_offsets_kernel<<<grid, 256, 0, stream>>>(n_images, gka, plane, raw, flow1, flow2, offset, mask);
     return cudaGetLastError();
 }
 

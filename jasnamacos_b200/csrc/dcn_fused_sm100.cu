@@ -26,6 +26,8 @@
 //   warp 1      MMA      : TMEM allocation; one thread issues tcgen05.mma
 //   warps 2-5   epilogue : TMEM -> registers, +bias, FP16, NCHW stores, Inf/NaN flag
 //   warps 6-13  producers: gather + bilinear + mask -> tcgen05.st into the A stage
+//                          (raw-input form: offsets and masks made from the offset
+//                          network's output and the flows as they are read)
 // Shapes this kernel takes are checked on the host (fused_supported()).
 //
 // Every mbarrier wait is bounded: on timeout the kernel records
@@ -89,6 +91,12 @@ struct Args {
     int nchunks;               // real chunks = OG * KA (the rest of the last block is zero)
     int tiles_per_image;
     int num_tiles;
+    // Raw-input form only: the two flows [N][2][plane] ((x, y) rows; deformable groups
+    // [0, OG/2) take flow1, the rest flow2) and the first mask-logit channel of the raw
+    // tensor, which then stands in for both the offset and the mask tensor.
+    const __half *flow1;
+    const __half *flow2;
+    int raw_mask_channel0;
 };
 
 __device__ uint32_t g_error_word;
@@ -111,6 +119,12 @@ struct StageRegs {
     uint32_t msk[4];     // half mask in the low 16 bits, 0 for padding chunks
 };
 
+// FromRaw = false: offsets and masks are inputs (the reference's DCN call).
+// FromRaw = true: tmap_off and tmap_msk both cover the offset network's raw output
+// [N][3*OG*KA][plane] (offset residues, then mask logits), and the producers apply
+// prepare_dcn_offsets_fp16 (MetalShader.swift:817-839) to each value they read, with
+// the flow of the chunk's deformable group (raw_offset / raw_mask).
+template <bool FromRaw>
 __global__ void __launch_bounds__(kThreads, 1)
     fused_dcn_kernel(const __grid_constant__ CUtensorMap tmap_off,
                      const __grid_constant__ CUtensorMap tmap_msk, const Args a) {
@@ -143,7 +157,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int g = j / p.KA;
             const int k = j - g * p.KA;
             const int ky = k / p.KW;
-            info = make_int4(g * p.H * (p.W + 1), ky * p.DH, (k - ky * p.KW) * p.DW, 1);
+            // w: nonzero for a real chunk; 2 when the raw-input form takes flow2 for its group
+            info = make_int4(g * p.H * (p.W + 1), ky * p.DH, (k - ky * p.KW) * p.DW, g < p.OG / 2 ? 1 : 2);
         }
         s.chunk[j] = info;
     }
@@ -182,7 +197,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                     }
                     mbar_arrive_expect_tx(&s.om_full[st], kStageTxBytes + kBBlockBytes);
                     tma_load_3d(&s.off[st][0][0], &tmap_off, &s.om_full[st], px0, kOffRows * sb, n);
-                    tma_load_3d(&s.msk[st][0][0], &tmap_msk, &s.om_full[st], px0, kMaskRows * sb, n);
+                    tma_load_3d(&s.msk[st][0][0], &tmap_msk, &s.om_full[st], px0,
+                                (FromRaw ? a.raw_mask_channel0 : 0) + kMaskRows * sb, n);
                     bulk_copy_g2s(s.b[st], a.packed_w + static_cast<size_t>(sb) * kBBlockBytes, kBBlockBytes,
                                   &s.om_full[st]);
                 }
@@ -296,6 +312,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         bool pf_valid = false;
         int pf_base_y = 0, pf_base_x = 0;
         const uint4 *pf_img = a.pairs;
+        float pf_f1x = 0.0f, pf_f1y = 0.0f, pf_f2x = 0.0f, pf_f2y = 0.0f;  // raw form: this pixel's flows
         auto enter_tile = [&](int local_tile) {
             const int tile = static_cast<int>(blockIdx.x) + local_tile * static_cast<int>(gridDim.x);
             const int n = tile / a.tiles_per_image;
@@ -307,6 +324,13 @@ __global__ void __launch_bounds__(kThreads, 1)
             pf_base_y = oy * p.SH - p.PH;
             pf_base_x = ox * p.SW - p.PW;
             pf_img = a.pairs + static_cast<size_t>(n) * p.OG * p.H * row_entries * 2;
+            if (FromRaw && pf_valid) {
+                const int64_t f = static_cast<int64_t>(n) * 2 * p.out_plane + px;
+                pf_f1x = __half2float(a.flow1[f]);
+                pf_f1y = __half2float(a.flow1[f + p.out_plane]);
+                pf_f2x = __half2float(a.flow2[f]);
+                pf_f2y = __half2float(a.flow2[f + p.out_plane]);
+            }
         };
 
         // Stage `itp` (the next one in order): read this pixel's offsets/masks of its 4
@@ -332,8 +356,15 @@ __global__ void __launch_bounds__(kThreads, 1)
                 R.frac[c4] = 0u;
                 R.msk[c4] = 0u;
                 if (valid && info.w) {
-                    const float off_y = __half2float(s.off[st][2 * c][r]);
-                    const float off_x = __half2float(s.off[st][2 * c + 1][r]);
+                    float off_y = __half2float(s.off[st][2 * c][r]);
+                    float off_x = __half2float(s.off[st][2 * c + 1][r]);
+                    __half mk = s.msk[st][c][r];
+                    if (FromRaw) {
+                        const bool second = info.w == 2;
+                        off_y = raw_offset(off_y, second ? pf_f2y : pf_f1y);
+                        off_x = raw_offset(off_x, second ? pf_f2x : pf_f1x);
+                        mk = __float2half_rn(raw_mask(__half2float(mk)));
+                    }
                     const float y = static_cast<float>(base_y + info.y) + off_y;
                     const float x = static_cast<float>(base_x + info.z) + off_x;
                     const int y0 = __float2int_rd(y);
@@ -347,7 +378,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     if (y0in) ldg_nc_256(e0, &R.v[c4][0]);
                     if (y1in) ldg_nc_256(e0 + 2 * row_entries, &R.v[c4][8]);
                     R.frac[c4] = pack_half2(__floats2half2_rn(y - static_cast<float>(y0), x - static_cast<float>(x0)));
-                    R.msk[c4] = static_cast<uint32_t>(__half_as_ushort(s.msk[st][c][r]));
+                    R.msk[c4] = static_cast<uint32_t>(__half_as_ushort(mk));
                 }
             }
             __syncwarp();
@@ -507,13 +538,17 @@ size_t fused_workspace_bytes(const Params &p) {
 // Once per device (with that device current): opt the kernel into its shared
 // memory size and look up the device address of the sticky error word.
 cudaError_t fused_prepare_device(uint32_t **err_word) {
-    cudaError_t e = cudaFuncSetAttribute(fused::fused_dcn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         static_cast<int>(sizeof(fused::Smem) + 1024));
-    if (e != cudaSuccess) return e;
-    cudaFuncAttributes attr;
-    e = cudaFuncGetAttributes(&attr, fused::fused_dcn_kernel);
-    if (e != cudaSuccess) return e;
-    if (attr.maxThreadsPerBlock < fused::kThreads) return cudaErrorInvalidConfiguration;
+    for (const void *fn : {reinterpret_cast<const void *>(fused::fused_dcn_kernel<false>),
+                           reinterpret_cast<const void *>(fused::fused_dcn_kernel<true>)}) {
+        cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             static_cast<int>(sizeof(fused::Smem) + 1024));
+        if (e != cudaSuccess) return e;
+        cudaFuncAttributes attr;
+        e = cudaFuncGetAttributes(&attr, fn);
+        if (e != cudaSuccess) return e;
+        if (attr.maxThreadsPerBlock < fused::kThreads) return cudaErrorInvalidConfiguration;
+    }
+    cudaError_t e;
     void *ptr = nullptr;
     e = cudaGetSymbolAddress(&ptr, fused::g_error_word);
     if (e != cudaSuccess) return e;
@@ -531,6 +566,27 @@ cudaError_t launch_regroup_c8(const Params &p, const SplitInput<__half> &input, 
     return cudaGetLastError();
 }
 
+namespace {
+
+fused::Args make_fused_args(const Params &p, const void *input_c8, const uint8_t *packed_w, const __half *bias,
+                            __half *output, uint32_t *flag, uint32_t *err) {
+    fused::Args a{};
+    a.p = p;
+    a.pairs = static_cast<const uint4 *>(input_c8);
+    a.packed_w = packed_w;
+    a.bias = bias;
+    a.out = output;
+    a.flag = flag;
+    a.err = err;
+    a.kb = fused_kblocks(p);
+    a.nchunks = p.OG * p.KA;
+    a.tiles_per_image = (p.out_plane + fused::BM - 1) / fused::BM;
+    a.num_tiles = p.N * a.tiles_per_image;
+    return a;
+}
+
+}  // namespace
+
 // The fused gather + tcgen05 kernel on a regrouped input, one persistent CTA per SM.
 cudaError_t launch_fused_grouped(const Params &p, const void *input_c8, const __half *offset,
                                  const __half *mask, const uint8_t *packed_w, const __half *bias,
@@ -541,20 +597,30 @@ cudaError_t launch_fused_grouped(const Params &p, const void *input_c8, const __
     if (!make_plane_map(&tmap_off, offset, p.out_plane, 2 * p.OG * p.KA, p.N, kOffRows) ||
         !make_plane_map(&tmap_msk, mask, p.out_plane, p.OG * p.KA, p.N, kMaskRows))
         return cudaErrorInvalidValue;
-    Args a;
-    a.p = p;
-    a.pairs = static_cast<const uint4 *>(input_c8);
-    a.packed_w = packed_w;
-    a.bias = bias;
-    a.out = output;
-    a.flag = flag;
-    a.err = err;
-    a.kb = fused_kblocks(p);
-    a.nchunks = p.OG * p.KA;
-    a.tiles_per_image = (p.out_plane + BM - 1) / BM;
-    a.num_tiles = p.N * a.tiles_per_image;
+    const Args a = make_fused_args(p, input_c8, packed_w, bias, output, flag, err);
     const int grid = a.num_tiles < sm_count ? a.num_tiles : sm_count;
-    fused_dcn_kernel<<<grid, kThreads, sizeof(Smem) + 1024, stream>>>(tmap_off, tmap_msk, a);
+    fused_dcn_kernel<false><<<grid, kThreads, sizeof(Smem) + 1024, stream>>>(tmap_off, tmap_msk, a);
+    return cudaGetLastError();
+}
+
+// The same kernel fed by the offset network's raw output [N][3*OG*KA][plane] and the two
+// flows [N][2][plane] (OG even): offsets and masks are made inside the producers.
+cudaError_t launch_fused_grouped_raw(const Params &p, const void *input_c8, const __half *raw,
+                                     const __half *flow1, const __half *flow2, const uint8_t *packed_w,
+                                     const __half *bias, __half *output, uint32_t *flag, int sm_count,
+                                     uint32_t *err, cudaStream_t stream) {
+    using namespace fused;
+    CUtensorMap tmap_off, tmap_msk;
+    const int raw_channels = 3 * p.OG * p.KA;
+    if (!make_plane_map(&tmap_off, raw, p.out_plane, raw_channels, p.N, kOffRows) ||
+        !make_plane_map(&tmap_msk, raw, p.out_plane, raw_channels, p.N, kMaskRows))
+        return cudaErrorInvalidValue;
+    Args a = make_fused_args(p, input_c8, packed_w, bias, output, flag, err);
+    a.flow1 = flow1;
+    a.flow2 = flow2;
+    a.raw_mask_channel0 = 2 * p.OG * p.KA;
+    const int grid = a.num_tiles < sm_count ? a.num_tiles : sm_count;
+    fused_dcn_kernel<true><<<grid, kThreads, sizeof(Smem) + 1024, stream>>>(tmap_off, tmap_msk, a);
     return cudaGetLastError();
 }
 

@@ -129,13 +129,6 @@ __device__ __forceinline__ void signal_abort(Smem &s, uint32_t *err) {
     atomicOr(err, kErrWaitTimeout);
 }
 
-// Hardware tanh approximation (sm_75+ tanh.approx.f32, ~2^-11 relative error).
-__device__ __forceinline__ float tanh_approx(float x) {
-    float y;
-    asm("tanh.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
-    return y;
-}
-
 __device__ __forceinline__ uint4 lds128(uint32_t addr) {
     uint4 v;
     asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(addr));
@@ -454,12 +447,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                         float off_x = __half2float(s.off[st][2 * k + 1][r]);
                         float mk = __half2float(s.msk[st][k][r]);
                         if (FromRaw) {
-                            // Rounded to FP16 like the reference's intermediate tensors.
-                            off_y = __half2float(__float2half_rn(10.0f * tanh_approx(off_y) +
-                                                                 __half2float(s.flow[st][1][r])));
-                            off_x = __half2float(__float2half_rn(10.0f * tanh_approx(off_x) +
-                                                                 __half2float(s.flow[st][0][r])));
-                            mk = __half2float(__float2half_rn(__fdividef(1.0f, 1.0f + __expf(-mk))));
+                            off_y = raw_offset(off_y, __half2float(s.flow[st][1][r]));
+                            off_x = raw_offset(off_x, __half2float(s.flow[st][0][r]));
+                            mk = raw_mask(mk);
                         }
                         const float y = (bfy[t] + tyf[i]) + off_y;
                         const float x = (bfx[t] + txf[i]) + off_x;
