@@ -367,6 +367,7 @@ def run_ours(args):
     kernel = {_native.DCN_PATH_SLAB_TC: "slab_dcn_kernel", _native.DCN_PATH_FUSED_TC: "fused_dcn_kernel"}.get(
         path, "direct_kernel")
     regroup_ms = None
+    plan = op.plan(shape) if not cfg["f32"] else None
     if tensor_path:
         op.regroup_input(shape, x, workspace=ws)
         kernel_ms = event_time_ms(graphed(lambda: op.forward_f16_grouped(shape, ws, off, msk, packed, b16, out=out,
@@ -375,11 +376,8 @@ def run_ours(args):
         regroup_ms = event_time_ms(graphed(lambda: op.regroup_input(shape, x, workspace=ws), use_graph),
                                    args.steps) / args.steps
         # pre-pass + tensor-core kernel, + the reduction pass when the slab kernel splits the
-        # deformable groups (batches with fewer 128-pixel tiles than SMs: the workspace then
-        # holds FP32 partial sums past the zero-bordered slabs)
-        slabs = shape.batch * shape.offset_groups * (shape.input_height + 2) * (shape.input_width + 2) * 16
-        split = path == _native.DCN_PATH_SLAB_TC and op.workspace_bytes(shape) > (slabs + 255) // 256 * 256
-        launches_per_step = 3 if split else 2
+        # deformable groups (batches with fewer 128-pixel tiles than SMs)
+        launches_per_step = plan["launches"]
     else:
         kernel_ms = ms / args.steps
         launches_per_step = 1 if cfg["f32"] else 2
@@ -489,7 +487,8 @@ def run_ours(args):
                        "parallelism": (f"tile shards x{world}, no data-path collective" if cfg["sharded"] else
                                        f"{world} independent replicas"),
                        "launch": "CUDA graph replay per step" if use_graph else "direct launches per step",
-                       "kernels_per_step": launches_per_step},
+                       "kernels_per_step": launches_per_step,
+                       "plan": plan},
             "roofline": {"bound": "hbm", "achieved": achieved_gbs, "peak": peaks["hbm_gbs"], "unit": "GB/s",
                          "frac": achieved_gbs / peaks["hbm_gbs"], "traffic": traffic,
                          "peak_source": f"{peak_kind} hbm_gbs", "kernel": kernel,

@@ -180,6 +180,27 @@ dcn_status dcn_prepack_weights(const dcn_shape *shape, const void *weight, dcn_d
  * read once; packed weights and workspaces must come from the same process. */
 dcn_path dcn_forward_f16_path(const dcn_shape *shape);
 
+/* How dcn_forward_f16 (and the raw form) launches a shape on the current device, for
+ * schedulers and profilers; no counterpart in the reference, whose host dispatches one
+ * Metal kernel per call.
+ *   path            as dcn_forward_f16_path
+ *   group_splits    slab path: deformable-group ranges per tile (> 1: a reduction pass
+ *                   adds the FP32 partial sums; DCN_B200_GROUP_SPLIT=0 turns it off)
+ *   tiles_per_unit  tensor-core paths: 128-pixel tiles per work unit
+ *   grid            CTAs of the tensor-core (or direct) kernel
+ *   prepass_images  images the regroup pre-pass converts before the kernel
+ *   launches        kernel launches per call (without the direct path's non-finite
+ *                   flag pass) */
+typedef struct dcn_plan {
+    int32_t path;
+    int32_t group_splits;
+    int32_t tiles_per_unit;
+    int32_t launches;
+    int64_t grid;
+    int64_t prepass_images;
+} dcn_plan;
+dcn_status dcn_forward_f16_plan(const dcn_shape *shape, dcn_plan *out);
+
 /* ---- fused FP16 path ----------------------------------------------------------
  * Replaces deform_conv2d_fp16_jasna_gather + deform_conv2d_fp16_jasna_simdgroup_gemm_fused
  * + flag_non_finite_fp16 (MetalShader.swift:299-463; host MetalRunner.swift:696-761;

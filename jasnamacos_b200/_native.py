@@ -81,6 +81,19 @@ class DcnIo(ctypes.Structure):
     ]
 
 
+class DcnPlan(ctypes.Structure):
+    """`struct dcn_plan`: how dcn_forward_f16 launches a shape on the current device."""
+
+    _fields_ = [
+        ("path", ctypes.c_int32),
+        ("group_splits", ctypes.c_int32),
+        ("tiles_per_unit", ctypes.c_int32),
+        ("launches", ctypes.c_int32),
+        ("grid", ctypes.c_int64),
+        ("prepass_images", ctypes.c_int64),
+    ]
+
+
 _P = ctypes.c_void_p
 _SHAPE = ctypes.POINTER(DcnShape)
 _IO = ctypes.POINTER(DcnIo)
@@ -101,6 +114,7 @@ PROTOTYPES = {
     "dcn_packed_weight_bytes": (ctypes.c_size_t, [_SHAPE]),
     "dcn_prepack_weights": (ctypes.c_int, [_SHAPE, _P, ctypes.c_int, ctypes.c_int, _P, _P]),
     "dcn_forward_f16_path": (ctypes.c_int, [_SHAPE]),
+    "dcn_forward_f16_plan": (ctypes.c_int, [_SHAPE, ctypes.POINTER(DcnPlan)]),
     "dcn_forward_f16_workspace_bytes": (ctypes.c_size_t, [_SHAPE]),
     "dcn_forward_f16": (
         ctypes.c_int,

@@ -49,6 +49,7 @@ cudaError_t launch_fused_grouped_raw(const Params &p, const void *input_c8, cons
                                      const __half *bias, __half *output, uint32_t *flag, int sm_count,
                                      uint32_t *err, cudaStream_t stream);
 bool slab_supported(const Params &p);
+void slab_plan(const Params &p, int sm_count, dcn_plan *out);
 size_t slab_workspace_bytes(const Params &p);
 size_t slab_packed_weight_bytes(const Params &p);
 cudaError_t slab_prepare_device();
@@ -263,6 +264,34 @@ dcn_status dcn_forward_f16_direct(const dcn_shape *shape, const void *input, con
 dcn_path dcn_forward_f16_path(const dcn_shape *shape) {
     if (validate(shape) != DCN_OK) return DCN_PATH_DIRECT;
     return select_path(make_params(*shape));
+}
+
+dcn_status dcn_forward_f16_plan(const dcn_shape *shape, dcn_plan *out) {
+    dcn_status st = validate(shape);
+    if (st != DCN_OK) return st;
+    if (out == nullptr) return DCN_ERR_INVALID_ARGUMENT;
+    DeviceInfo *dev = nullptr;
+    if ((st = current_device(&dev)) != DCN_OK) return st;
+    const Params p = make_params(*shape);
+    *out = dcn_plan{};
+    const dcn_path path = select_path(p);
+    if (path == DCN_PATH_SLAB_TC) {
+        slab_plan(p, dev->sm_count, out);
+        return DCN_OK;
+    }
+    out->path = path;
+    out->group_splits = 1;
+    out->tiles_per_unit = 1;
+    if (path == DCN_PATH_FUSED_TC) {
+        const int64_t tiles = static_cast<int64_t>(p.N) * ((p.out_plane + 127) / 128);
+        out->grid = tiles < dev->sm_count ? tiles : dev->sm_count;
+        out->prepass_images = p.N;
+        out->launches = 2;
+    } else {
+        out->grid = (static_cast<int64_t>(p.N) * p.out_plane + 15) / 16 * p.G * ((p.opg + 63) / 64);
+        out->launches = 1;
+    }
+    return DCN_OK;
 }
 
 size_t dcn_packed_weight_bytes(const dcn_shape *shape) {

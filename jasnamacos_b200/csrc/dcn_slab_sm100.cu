@@ -828,6 +828,17 @@ cudaError_t launch_split_reduce(const Params &p, const slab::Args &a, cudaStream
 
 }  // namespace
 
+// Launch plan of the slab path (dcn_forward_f16_plan).
+void slab_plan(const Params &p, int sm_count, dcn_plan *out) {
+    const slab::Args a = make_slab_args(p, nullptr, nullptr, nullptr, nullptr, nullptr, sm_count, nullptr);
+    out->path = DCN_PATH_SLAB_TC;
+    out->group_splits = a.splits;
+    out->tiles_per_unit = a.tiles_per_unit;
+    out->launches = a.splits > 1 ? 3 : 2;
+    out->grid = a.num_units < sm_count ? a.num_units : sm_count;
+    out->prepass_images = p.N;
+}
+
 cudaError_t launch_slab_grouped(const Params &p, const void *slabs, const __half *offset, const __half *mask,
                                 const uint8_t *packed_w, const __half *bias, __half *output, uint32_t *flag,
                                 int sm_count, uint32_t *err, cudaStream_t stream) {

@@ -259,6 +259,16 @@ class CudaDeformConv:
     def path(self, shape: DeformConvShape) -> int:
         return self.lib.dcn_forward_f16_path(ctypes.byref(shape.to_c()))
 
+    def plan(self, shape: DeformConvShape) -> dict:
+        """dcn_forward_f16_plan: path, group splits, tiles per unit, launches per call, grid and
+        images converted by the pre-pass, on this operator's device."""
+        torch = _torch()
+        out = _native.DcnPlan()
+        with torch.cuda.device(self.device):
+            st = self.lib.dcn_forward_f16_plan(ctypes.byref(shape.to_c()), ctypes.byref(out))
+        raise_for_status(st, "dcn_forward_f16_plan")
+        return {name: int(getattr(out, name)) for name, _ in _native.DcnPlan._fields_}
+
     def packed_weight_bytes(self, shape: DeformConvShape) -> int:
         return int(self.lib.dcn_packed_weight_bytes(ctypes.byref(shape.to_c())))
 

@@ -108,3 +108,26 @@ def test_stream_ordering_on_a_side_stream(cuda_op):
     side.synchronize()
     assert torch.equal(base, out)
     assert ctypes.sizeof(ctypes.c_void_p) == 8
+
+
+@pytest.mark.parametrize("shape,path,splits,launches", [
+    (DeformConvShape.jasna_propagation(1, 64, 64), _native.DCN_PATH_SLAB_TC, 4, 3),
+    (DeformConvShape.jasna_propagation(2048, 64, 64), _native.DCN_PATH_SLAB_TC, 1, 2),
+    (DeformConvShape.jasna_propagation(1, 270, 480), _native.DCN_PATH_FUSED_TC, 1, 2),
+    (DeformConvShape.jasna_propagation(2, 5, 7), _native.DCN_PATH_DIRECT, 1, 1),
+], ids=["one_tile_image", "config4", "config3", "direct"])
+def test_launch_plan(cuda_op, shape, path, splits, launches):
+    """dcn_forward_f16_plan agrees with the path query and the workspace layout: a group
+    split (a reduction pass and FP32 partials past the slabs) only for batches with fewer
+    128-pixel tiles than SMs, persistent grids of at most one CTA per SM."""
+    import torch
+
+    plan = cuda_op.plan(shape)
+    assert plan["path"] == cuda_op.path(shape) == path
+    assert plan["group_splits"] == splits and plan["launches"] == launches
+    sms = torch.cuda.get_device_properties(0).multi_processor_count
+    if path != _native.DCN_PATH_DIRECT:
+        assert 1 <= plan["grid"] <= sms and plan["prepass_images"] == shape.batch
+    if path == _native.DCN_PATH_SLAB_TC:
+        slabs = shape.batch * shape.offset_groups * (shape.input_height + 2) * (shape.input_width + 2) * 16
+        assert (cuda_op.workspace_bytes(shape) > (slabs + 255) // 256 * 256) == (splits > 1)
