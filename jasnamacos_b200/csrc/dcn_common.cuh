@@ -181,6 +181,36 @@ __device__ __forceinline__ void prefetch_tensor_map(const void *tensor_map) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(tensor_map) : "memory");
 }
 
+// ---- programmatic dependent launch -----------------------------------------------
+// The kernels after the first of an operator call are launched with programmatic stream
+// serialization (launch_dependent): their CTAs may become resident while the previous
+// kernel of the call is still running, do the set-up that touches no global memory
+// (mbarrier init, tensor-memory allocation, tensor-map prefetch) and then block in
+// grid_dependency_wait(), which returns only when every prerequisite grid has completed
+// and its memory operations are visible -- so results are those of plain stream order,
+// with the launch latency and the set-up hidden.  A kernel followed by one of ours calls
+// allow_dependent_launch() to let that launch begin early.
+__device__ __forceinline__ void grid_dependency_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void allow_dependent_launch() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+template <typename... KArgs, typename... Args>
+cudaError_t launch_dependent(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                             Args &&...args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, static_cast<Args &&>(args)...);
+}
+
 // ---- offset producer of the raw-input form ---------------------------------------
 // prepare_dcn_offsets_fp16 (Sources/JasnaMetalPoC/MetalShader.swift:817-839) as the
 // tensor-core kernels evaluate it inside their producers: offset = 10*tanh(residue) + flow,

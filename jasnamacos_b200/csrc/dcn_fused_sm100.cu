@@ -150,7 +150,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         s.abort_flag = 0;
         fence_mbarrier_init();
     }
-    if (threadIdx.x < BN) s.bias[threadIdx.x] = __half2float(a.bias[threadIdx.x]);
     for (int j = threadIdx.x; j < a.kb * kChunksPerStage; j += blockDim.x) {
         int4 info = make_int4(0, 0, 0, 0);
         if (j < a.nchunks) {
@@ -170,6 +169,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         prefetch_tensor_map(&tmap_off);
         prefetch_tensor_map(&tmap_msk);
     }
+    // Launched as a dependent of the regroup pre-pass: no global memory before this.
+    grid_dependency_wait();
+    if (threadIdx.x < BN) s.bias[threadIdx.x] = __half2float(a.bias[threadIdx.x]);
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
@@ -450,6 +452,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 // images n (so no 64-bit division per thread).
 __global__ void __launch_bounds__(256) regroup_pairs_kernel(const SplitInput<__half> in,
                                                              uint4 *__restrict__ out, int N, int H, int W) {
+    allow_dependent_launch();  // the fused kernel may start its set-up
     const int entries = H * (W + 1);
     const int i = blockIdx.x * blockDim.x + threadIdx.x;  // entry index within the plane
     if (i >= entries) return;
@@ -599,8 +602,8 @@ cudaError_t launch_fused_grouped(const Params &p, const void *input_c8, const __
         return cudaErrorInvalidValue;
     const Args a = make_fused_args(p, input_c8, packed_w, bias, output, flag, err);
     const int grid = a.num_tiles < sm_count ? a.num_tiles : sm_count;
-    fused_dcn_kernel<false><<<grid, kThreads, sizeof(Smem) + 1024, stream>>>(tmap_off, tmap_msk, a);
-    return cudaGetLastError();
+    return launch_dependent(fused_dcn_kernel<false>, dim3(grid), dim3(kThreads), sizeof(Smem) + 1024, stream, tmap_off,
+                            tmap_msk, a);
 }
 
 // The same kernel fed by the offset network's raw output [N][3*OG*KA][plane] and the two
@@ -620,8 +623,8 @@ cudaError_t launch_fused_grouped_raw(const Params &p, const void *input_c8, cons
     a.flow2 = flow2;
     a.raw_mask_channel0 = 2 * p.OG * p.KA;
     const int grid = a.num_tiles < sm_count ? a.num_tiles : sm_count;
-    fused_dcn_kernel<true><<<grid, kThreads, sizeof(Smem) + 1024, stream>>>(tmap_off, tmap_msk, a);
-    return cudaGetLastError();
+    return launch_dependent(fused_dcn_kernel<true>, dim3(grid), dim3(kThreads), sizeof(Smem) + 1024, stream, tmap_off,
+                            tmap_msk, a);
 }
 
 }  // namespace dcn

@@ -185,7 +185,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         s.abort_flag = 0;
         fence_mbarrier_init();
     }
-    if (threadIdx.x < BN) s.bias[threadIdx.x] = __half2float(a.bias[threadIdx.x]);
     if (threadIdx.x < kTaps) {
         const int ky = threadIdx.x / p.KW;
         s.tap[threadIdx.x] = make_int2(ky * p.DH, (static_cast<int>(threadIdx.x) - ky * p.KW) * p.DW);
@@ -202,6 +201,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             prefetch_tensor_map(&tmap_flow2);
         }
     }
+    // Launched as a dependent of the regroup pre-pass: no global memory before this.
+    grid_dependency_wait();
+    if (a.splits > 1) allow_dependent_launch();  // the reduction pass may start its set-up
+    if (threadIdx.x < BN) s.bias[threadIdx.x] = __half2float(a.bias[threadIdx.x]);
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
@@ -531,6 +534,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 // over the images n (so no 64-bit division per thread).
 __global__ void __launch_bounds__(256) regroup_slabs_kernel(const SplitInput<__half> in, uint4 *__restrict__ out,
                                                              int N, int H, int W) {
+    allow_dependent_launch();  // the slab kernel may start its set-up
     const int sw = W + 2;
     const int positions = (H + 2) * sw;
     const int pos = blockIdx.x * blockDim.x + threadIdx.x;
@@ -562,6 +566,7 @@ __global__ void __launch_bounds__(256) regroup_slabs_kernel(const SplitInput<__h
 __global__ void __launch_bounds__(256) slab_reduce_kernel(Params p, const float *__restrict__ partial, int splits,
                                                            const __half *__restrict__ bias, __half *__restrict__ out,
                                                            uint32_t *__restrict__ flag) {
+    grid_dependency_wait();  // the slab kernel's partial sums
     const int64_t per_split = static_cast<int64_t>(p.N) * BN * p.out_plane;
     const int64_t i = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) * 4;
     bool bad = false;
@@ -598,6 +603,7 @@ __global__ void __launch_bounds__(256) slab_reduce_kernel(Params p, const float 
 // two border columns 0 and W+1; the border rows 0 and H+1 are all zeros.
 __global__ void __launch_bounds__(256) regroup_slabs_x4_kernel(const SplitInput<__half> in, uint4 *__restrict__ out,
                                                                 int N, int H, int W) {
+    allow_dependent_launch();  // the slab kernel may start its set-up
     const int per_row = W / 4 + 1;
     const int t = blockIdx.x * blockDim.x + threadIdx.x;
     if (t >= (H + 2) * per_row) return;
@@ -821,9 +827,8 @@ cudaError_t launch_split_reduce(const Params &p, const slab::Args &a, cudaStream
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess || a.splits == 1) return e;
     const int64_t quads = static_cast<int64_t>(p.N) * slab::BN * p.out_plane / 4;
-    slab::slab_reduce_kernel<<<static_cast<unsigned>((quads + 255) / 256), 256, 0, stream>>>(p, a.partial, a.splits,
-                                                                                             a.bias, a.out, a.flag);
-    return cudaGetLastError();
+    return launch_dependent(slab::slab_reduce_kernel, dim3(static_cast<unsigned>((quads + 255) / 256)), dim3(256), 0,
+                            stream, p, static_cast<const float *>(a.partial), a.splits, a.bias, a.out, a.flag);
 }
 
 }  // namespace
@@ -849,7 +854,9 @@ cudaError_t launch_slab_grouped(const Params &p, const void *slabs, const __half
         return cudaErrorInvalidValue;
     const Args a = make_slab_args(p, slabs, packed_w, bias, output, flag, sm_count, err);
     const int grid = a.num_units < sm_count ? a.num_units : sm_count;
-    slab_dcn_kernel<false><<<grid, kThreads, slab_smem_bytes(p), stream>>>(tmap_off, tmap_msk, tmap_off, tmap_msk, a);
+    cudaError_t e = launch_dependent(slab_dcn_kernel<false>, dim3(grid), dim3(kThreads), slab_smem_bytes(p), stream,
+                                     tmap_off, tmap_msk, tmap_off, tmap_msk, a);
+    if (e != cudaSuccess) return e;
     return launch_split_reduce(p, a, stream);
 }
 
@@ -868,7 +875,9 @@ cudaError_t launch_slab_grouped_raw(const Params &p, const void *slabs, const __
         return cudaErrorInvalidValue;
     const Args a = make_slab_args(p, slabs, packed_w, bias, output, flag, sm_count, err);
     const int grid = a.num_units < sm_count ? a.num_units : sm_count;
-    slab_dcn_kernel<true><<<grid, kThreads, slab_smem_bytes(p), stream>>>(tmap_off, tmap_msk, tmap_f1, tmap_f2, a);
+    cudaError_t e = launch_dependent(slab_dcn_kernel<true>, dim3(grid), dim3(kThreads), slab_smem_bytes(p), stream,
+                                     tmap_off, tmap_msk, tmap_f1, tmap_f2, a);
+    if (e != cudaSuccess) return e;
     return launch_split_reduce(p, a, stream);
 }
 
