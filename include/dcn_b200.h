@@ -333,6 +333,13 @@ dcn_status dcn_forward_f16_static_scratch(const dcn_shape *shape, const void *in
  * for the current device and clears the word (synchronises the device). */
 dcn_status dcn_device_error(void);
 
+/* A check of that failure path, with no counterpart in the reference: one CTA waits, with
+ * the operator kernels' bounded-wait code and a limit of `limit_us` microseconds (1 to
+ * 10,000,000), on an mbarrier that nothing arrives on.  The wait must run out and record
+ * the timeout in the device error word, so that the next dcn_device_error() returns
+ * DCN_ERR_DEVICE_TIMEOUT while the CUDA context stays usable.  Asynchronous on `stream`. */
+dcn_status dcn_check_wait_timeout(uint32_t limit_us, dcn_stream stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -29,6 +29,7 @@ cudaError_t launch_flag_non_finite(const __half *values, int64_t count, uint32_t
                                    cudaStream_t stream);
 cudaError_t launch_flag_non_finite_rows(const __half *values, int64_t rows, int64_t row_len, int64_t row_stride,
                                         uint32_t *flag, int sm_count, cudaStream_t stream);
+cudaError_t launch_check_wait_timeout(uint64_t limit_ns, uint32_t *err, cudaStream_t stream);
 cudaError_t launch_prepare_offsets(int64_t n_images, int gka, int64_t plane, const __half *raw, const __half *flow1,
                                    const __half *flow2, __half *offset, __half *mask, cudaStream_t stream);
 cudaError_t launch_slab_grouped_raw(const Params &p, const void *slabs, const __half *raw, const __half *flow1,
@@ -562,6 +563,15 @@ dcn_status dcn_device_error(void) {
         return DCN_ERR_DEVICE_TIMEOUT;
     }
     return DCN_OK;
+}
+
+dcn_status dcn_check_wait_timeout(uint32_t limit_us, dcn_stream stream) {
+    if (limit_us == 0 || limit_us > 10000000u) return DCN_ERR_INVALID_ARGUMENT;
+    DeviceInfo *dev = nullptr;
+    dcn_status st = current_device(&dev);
+    if (st != DCN_OK) return st;
+    return from_cuda(launch_check_wait_timeout(static_cast<uint64_t>(limit_us) * 1000u, dev->err_word,
+                                               reinterpret_cast<cudaStream_t>(stream)));
 }
 
 }  // extern "C"

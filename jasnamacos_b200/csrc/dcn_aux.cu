@@ -58,7 +58,23 @@ __global__ void __launch_bounds__(256) prepare_offsets_kernel(int64_t n_images, 
     }
 }
 
+// One thread waits on an mbarrier that expects an arrival nobody makes, with the bounded
+// wait of the operator kernels; when the wait runs out it records the timeout the way they
+// do (one bit in the device error word) and returns.
+__global__ void check_wait_timeout_kernel(uint64_t limit_ns, uint32_t *err) {
+    __shared__ uint64_t bar;
+    if (threadIdx.x != 0) return;
+    mbar_init(&bar, 1);
+    fence_mbarrier_init();
+    if (!mbar_wait_bounded(&bar, 0, nullptr, 0, limit_ns)) atomicOr(err, kErrWaitTimeout);
+}
+
 }  // namespace
+
+cudaError_t launch_check_wait_timeout(uint64_t limit_ns, uint32_t *err, cudaStream_t stream) {
+    check_wait_timeout_kernel<<<1, 32, 0, stream>>>(limit_ns, err);
+    return cudaGetLastError();
+}
 
 cudaError_t launch_flag_non_finite_rows(const __half *values, int64_t rows, int64_t row_len, int64_t row_stride,
                                         uint32_t *flag, int sm_count, cudaStream_t stream) {

@@ -140,8 +140,10 @@ __device__ __forceinline__ bool mbar_try_wait_suspend(uint64_t *bar, uint32_t pa
 // their polling does not take issue slots and shared-memory cycles).  Critical
 // waiters poll with a hardware suspend hint instead, which wakes them as soon as
 // the phase completes.
+// `limit_ns` replaces kWaitLimitNs for callers that want a shorter bound.
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t parity,
-                                                  volatile int *abort, uint32_t backoff_ns = 0) {
+                                                  volatile int *abort, uint32_t backoff_ns = 0,
+                                                  uint64_t limit_ns = kWaitLimitNs) {
     if (mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = global_timer_ns();
     while (true) {
@@ -152,7 +154,7 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t parity
             return true;
         }
         if (abort != nullptr && *abort) return false;
-        if (global_timer_ns() - t0 > kWaitLimitNs) return false;
+        if (global_timer_ns() - t0 > limit_ns) return false;
     }
 }
 

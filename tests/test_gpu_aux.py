@@ -131,3 +131,36 @@ def test_launch_plan(cuda_op, shape, path, splits, launches):
     if path == _native.DCN_PATH_SLAB_TC:
         slabs = shape.batch * shape.offset_groups * (shape.input_height + 2) * (shape.input_width + 2) * 16
         assert (cuda_op.workspace_bytes(shape) > (slabs + 255) // 256 * 256) == (splits > 1)
+
+
+def test_bounded_wait_timeout_is_reported_and_context_survives(cuda_op):
+    """The failure path of every bounded device wait, without a fault: a wait that nothing
+    completes runs out after its limit, the kernel records the timeout in the device error
+    word and returns, the host reads DCN_ERR_DEVICE_TIMEOUT once (the read clears it), and
+    the same context then runs the operator correctly."""
+    import time
+
+    import torch
+
+    from jasnamacos_b200.deform_conv import DeviceTimeout
+
+    assert cuda_op.lib.dcn_check_wait_timeout(0, None) == _native.DCN_ERR_INVALID_ARGUMENT
+    assert cuda_op.lib.dcn_device_error() == _native.DCN_OK
+    t0 = time.perf_counter()
+    assert cuda_op.lib.dcn_check_wait_timeout(100_000, None) == _native.DCN_OK  # 100 ms limit
+    with pytest.raises(DeviceTimeout):
+        cuda_op.device_error()  # synchronises: the wait has run out by now
+    elapsed = time.perf_counter() - t0
+    assert 0.09 <= elapsed < 5.0, elapsed
+    assert cuda_op.lib.dcn_device_error() == _native.DCN_OK, "the error word is cleared by the read"
+
+    inp = synthetic.generate(1)
+    s = inp.shape
+    x, off, msk, w, b = [torch.from_numpy(a).cuda() for a in inp.tensors_f16()]
+    out = cuda_op.forward_f16(s, x, off, msk, cuda_op.prepack(s, w), b)
+    torch.cuda.synchronize()
+    cuda_op.device_error()
+    q = inp.quantized()
+    ref = oracle.run(s, q.input, q.offset, q.mask, q.weight, q.bias)
+    d = np.abs(out.float().cpu().numpy() - ref)
+    assert d.max() <= 2e-2 and d.mean() <= 2e-3, (float(d.max()), float(d.mean()))
