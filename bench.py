@@ -39,6 +39,15 @@ TILE_H = TILE_W = 64
 BYTES_PER_PX = 256 + 576 + 288 + 128  # input + offset + mask + output, FP16
 FLOPS_PER_PX = 2 * 64 * 1152
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+# What bounds each kernel below the HBM and tensor rooflines, from ncu captures of this build
+# (not measured by this script).
+LIMITERS = {
+    "slab_dcn_kernel": "shared-memory data pipe: 77.6% of peak LSU wavefronts (256-tile config-4 case); four random "
+                       "16-byte loads per bilinear sample, about half of the wavefronts are bank-conflict replays",
+    "fused_dcn_kernel": "L1 data pipe: ~72% of peak LSU wavefronts (config 3); scattered 32-byte corner-pair "
+                        "loads from global memory, L1 hit rate ~8%",
+    "direct_kernel": "L1 data pipe and latency: one scattered 4-byte global load per bilinear corner",
+}
 
 
 def load_peaks():
@@ -496,7 +505,8 @@ def run_ours(args):
                          "algorithmic_bytes_per_px": bytes_per_px,
                          "tensor_tflops": tensor_tflops if tensor_path else None,
                          "tensor_frac": tensor_tflops / peaks["bf16_tflops"] if tensor_path else None,
-                         "tensor_peak_source": f"{peak_kind} bf16_tflops (burst)"},
+                         "tensor_peak_source": f"{peak_kind} bf16_tflops (burst)",
+                         "limiter": LIMITERS.get(kernel)},
             "cpu_baseline": cpu,
             "e2e": e2e,
             "raw_form": raw_form,
