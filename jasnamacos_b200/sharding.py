@@ -17,13 +17,15 @@ def shard_range(total: int, rank: int, world: int) -> tuple[int, int]:
     return total * rank // world, total * (rank + 1) // world
 
 
-def gather_to_root(local, total_tiles: int, per_tile: int, dist, root: int = 0):
+def gather_to_root(local, total_tiles: int, per_tile: int, dist, root: int = 0, out=None):
     """Collects every rank's shard of a [tiles * per_tile] output onto `root`.
 
     `local` is this rank's contiguous shard (a torch tensor); `dist` is
     torch.distributed with an initialised process group (NCCL for CUDA tensors, gloo for
-    CPU).  Ranks exchange point-to-point (shards may differ in size by one tile).
-    Returns the full tensor on root and None elsewhere.  Every rank takes the same steps.
+    CPU).  Ranks exchange point-to-point (shards may differ in size by one tile); root posts
+    all its receives in one batch, so the shards arrive concurrently (over NVLink for NCCL).
+    `out` (root only, optional) receives the full tensor.  Returns the full tensor on root
+    and None elsewhere.  Every rank takes the same steps.
     """
     import torch
 
@@ -32,14 +34,20 @@ def gather_to_root(local, total_tiles: int, per_tile: int, dist, root: int = 0):
     if local.numel() != (e - b) * per_tile:
         raise ValueError("local shard has the wrong size")
     if rank != root:
-        dist.send(local.contiguous(), dst=root)
+        for req in dist.batch_isend_irecv([dist.P2POp(dist.isend, local.contiguous(), root)]):
+            req.wait()
         return None
-    full = torch.empty(total_tiles * per_tile, dtype=local.dtype, device=local.device)
+    full = out if out is not None else torch.empty(total_tiles * per_tile, dtype=local.dtype, device=local.device)
+    if full.numel() != total_tiles * per_tile:
+        raise ValueError("out has the wrong size")
     full[b * per_tile:e * per_tile].copy_(local)
+    ops = []
     for src in range(world):
         if src == root:
             continue
         sb, se = shard_range(total_tiles, src, world)
-        view = full[sb * per_tile:se * per_tile]
-        dist.recv(view, src=src)
+        ops.append(dist.P2POp(dist.irecv, full[sb * per_tile:se * per_tile], src))
+    if ops:
+        for req in dist.batch_isend_irecv(ops):
+            req.wait()
     return full
