@@ -416,6 +416,29 @@ def run_ours(args):
                             "computed inside the kernel (prepare_dcn_offsets_fp16 fused)"}
         del raw, f1, f2, wsr
 
+    # ---- final gather of every shard's output to rank 0 (N > 1, after the timed step) ---
+    gather = None
+    if pg is not None and cfg["sharded"]:
+        from jasnamacos_b200 import sharding
+
+        per_image = base_shape.output_count
+        full = torch.empty(total_images * per_image, dtype=out.dtype, device=dev) if rank == 0 else None
+        gather_step = lambda: sharding.gather_to_root(out, total_images, per_image, pg, out=full)  # noqa: E731
+        gather_step()  # connection set-up, untimed
+        torch.cuda.synchronize(dev)
+        barrier(pg)
+        g_ms = max_over_ranks(event_time_ms(gather_step, 3), pg) / 3
+        own = (i_end - i_begin) if rank == 0 else 0
+        recv_bytes = (total_images - own) * per_image * out.element_size() if rank == 0 else 0
+        recv_bytes = int(max_over_ranks(float(recv_bytes), pg))
+        gather = {"ms": g_ms, "bytes_to_root": recv_bytes, "GB_s": recv_bytes / (g_ms * 1e-3) / 1e9,
+                  "value_with_gather": job_px / ((ms_per_step + g_ms) * 1e-3) / 1e6, "unit": "Mpx/s",
+                  "what": "every rank's output shard to rank 0 (NCCL point-to-point, receives posted together); "
+                          "not part of the timed step"}
+        del full
+        torch.cuda.synchronize(dev)
+        barrier(pg)
+
     # ---- end to end through the host-buffer API ------------------------------------
     e2e = None
     if not args.no_e2e:
@@ -510,6 +533,7 @@ def run_ours(args):
             "cpu_baseline": cpu,
             "e2e": e2e,
             "raw_form": raw_form,
+            "gather": gather,
             "gpu_launches": launches_per_step * args.steps,
             "clocks": clocks,
             "nonfinite_flag": nonfinite,
