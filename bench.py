@@ -1,6 +1,6 @@
 """DCNv2 benchmark: output Mpixels/s of the fused FP16 B200 operator.
 
-Workload (config 4 of the round's benchmark set): N=2048 FP16 tiles of 128x64x64 -> 64x64x64,
+Workload (config 4 of the DCNv2 benchmark set): N=2048 FP16 tiles of 128x64x64 -> 64x64x64,
 3x3, pad 1, 16 deformable groups, offsets 10*tanh(N(0,1)) + per-pixel flow U(-16,16), mask
 sigmoid(N(0,1)); the 2048 tiles are sharded evenly over the GPUs (total work fixed, so
 "scaling": "strong"), no data-path collective.  Inputs are synthetic, generated on each GPU
@@ -9,8 +9,8 @@ from a fixed seed.  One step = one pass of the operator (C ABI dcn_forward_f16: 
 GPU, far more than the 126 MB L2, so no separate L2 flush is needed.
 
 Reported: `value` (inputs resident in HBM, CUDA events on the launching stream, max over
-ranks), `e2e` (the host-buffer API forward_f16_host: pinned host -> device copies, kernels,
-device -> host output and flag read, every step), `roofline` (the fused kernel timed alone,
+ranks), `e2e` (the C ABI's host-buffer entry dcn_forward_f16_host: pinned host -> device copies,
+kernels, device -> host output and flag read, every step), `roofline` (the fused kernel timed alone,
 algorithmic bytes 1248 B/px), `cpu_baseline` (the literal CPU reference loop on a bounded
 sample of the same tiles, rank 0 at N=1).  `--impl reference` times only that CPU reference
 (the reference implementation of this path is CPU code; its GPU code is Metal).
@@ -244,6 +244,68 @@ def run_reference_arm(args):
     return 0
 
 
+# ----------------------------------------------------------------------------- parity
+
+
+F16_GATES = {"max_abs": 2e-2, "mean_abs": 2e-3}
+
+
+def parity_check(config, shape, first, total_images, world, x, off, msk, out, w, b, pg):
+    """The timed output checked against the CPU oracle (the restatement of DeformConvCPU.run,
+    DeformConv.swift:75-138) on a deterministic sample of the benchmarked images, after the
+    timed region.  Tile batches: the tiles of sharding.sample_tiles spread over eight equal
+    ranges of the batch (16 per range for config 4, 2 for config 2), each rank checking the
+    sampled tiles of its own shard; single-image configurations: the image itself.  The oracle
+    is only the checker here.  Returns the sample, the worst and mean absolute error over all
+    ranks and the gate verdict (FP16: max abs <= 2e-2, mean abs <= 2e-3; FP32: bit-identical)."""
+    import numpy as np
+    import torch
+
+    import oracle
+    from jasnamacos_b200 import sharding, synthetic
+
+    if config in synthetic.SHARDED_CONFIGS:
+        sample = sharding.sample_tiles(total_images, 8, 16 if config == 4 else 2)
+    else:
+        sample = [0]
+    mine = [t - first for t in sample if first <= t < first + shape.batch]
+    per = shape.with_batch(1)
+    worst, abs_sum, count, mismatches = 0.0, 0.0, 0, 0
+    if mine:
+        idx = torch.tensor(mine, device=out.device)
+
+        def rows(t, n):
+            return t.view(shape.batch, n).index_select(0, idx).float().cpu().numpy().reshape(-1)
+
+        sub = per.with_batch(len(mine))
+        threads = max(1, oracle.host_threads() // world)
+        ref = oracle.run(sub, rows(x, per.input_count), rows(off, per.offset_count), rows(msk, per.mask_count),
+                         w.float().cpu().numpy(), b.float().cpu().numpy(), threads=threads)
+        got = rows(out, per.output_count)
+        d = np.abs(got.astype(np.float64) - ref.astype(np.float64))
+        worst = float(d.max()) if np.isfinite(d).all() else float("inf")
+        abs_sum, count = float(d.sum()), int(d.size)
+        mismatches = int(np.count_nonzero(got != ref))
+    if pg is not None:
+        t = torch.tensor([worst], dtype=torch.float64, device=out.device)
+        pg.all_reduce(t, op=pg.ReduceOp.MAX)
+        worst = float(t.item())
+        t = torch.tensor([abs_sum, float(count), float(mismatches)], dtype=torch.float64, device=out.device)
+        pg.all_reduce(t, op=pg.ReduceOp.SUM)
+        abs_sum, count, mismatches = float(t[0]), int(t[1]), int(t[2])
+    mean = abs_sum / max(count, 1)
+    f32 = out.dtype == torch.float32
+    line = {"sampled_images": len(sample), "sample": "sharding.sample_tiles over 8 ranges of the batch"
+            if config in synthetic.SHARDED_CONFIGS else "image 0 of every replica",
+            "outputs_compared": count, "max_abs": worst, "mean_abs": mean,
+            "checker": "oracle (C restatement of DeformConvCPU.run) on the same FP16-quantised inputs"}
+    if f32:
+        line.update(gate="bit-identical", mismatched_outputs=mismatches, passed=mismatches == 0)
+    else:
+        line.update(gate=F16_GATES, passed=worst <= F16_GATES["max_abs"] and mean <= F16_GATES["mean_abs"])
+    return line
+
+
 # ----------------------------------------------------------------------------- our arm
 
 
@@ -314,23 +376,15 @@ def run_ours(args):
     cfg = CONFIGS[args.config]
 
     total_images = args.tiles if args.config == 4 else cfg["images"]
-    if cfg["sharded"]:
-        i_begin, i_end = total_images * rank // world, total_images * (rank + 1) // world
-        job_images = total_images
-    else:
-        i_begin, i_end = 0, total_images
-        job_images = total_images * world
+    job_images = total_images if cfg["sharded"] else total_images * world
     base_shape = synthetic.config_shape(args.config, batch=1)
-    shape = base_shape.with_batch(i_end - i_begin)
+    # The rank's images and their inputs (seeded by the shard's first image, so a parity
+    # check can rebuild any benchmarked tile).
+    shape, i_begin, x, off, msk, w, b = synthetic.bench_inputs(args.config, rank, world, dev,
+                                                               args.tiles if args.config == 4 else None)
+    i_end = i_begin + shape.batch
     px_per_step = shape.output_pixels
     job_px = job_images * base_shape.output_pixels
-    if cfg["f32"]:
-        x, off, msk, w, b = synthetic.device_gaussian_batch(shape, seed=1000 + i_begin, device=dev,
-                                                            dtype=torch.float32)
-    elif cfg["flow"] is None:
-        x, off, msk, w, b = synthetic.device_gaussian_batch(shape, seed=1000 + i_begin, device=dev)
-    else:
-        x, off, msk, w, b = synthetic.device_batch(shape, cfg["flow"], seed=1000 + i_begin, device=dev)
     path = _native.DCN_PATH_DIRECT if cfg["f32"] else op.path(shape)
     out = torch.empty(shape.output_count, dtype=torch.float32 if cfg["f32"] else torch.float16, device=dev)
     flag = torch.zeros(1, dtype=torch.int32, device=dev)
@@ -370,6 +424,12 @@ def run_ours(args):
     value = job_px / (ms_per_step * 1e-3) / 1e6  # whole job, Mpx/s
     op.device_error()
     nonfinite = int(flag.item())
+
+    # ---- parity of the timed output against the CPU oracle (off the timed region) -------
+    parity = None
+    if not args.no_parity:
+        parity = parity_check(args.config, shape, i_begin, total_images, world, x, off, msk, out,
+                              w32 if cfg["f32"] else w16, b32 if cfg["f32"] else b16, pg)
 
     # ---- dominant kernel alone, for the roofline ----------------------------------
     tensor_path = path in (_native.DCN_PATH_SLAB_TC, _native.DCN_PATH_FUSED_TC)
@@ -456,8 +516,9 @@ def run_ours(args):
                 h_out.copy_(out, non_blocking=True)
                 torch.cuda.current_stream().synchronize()
         else:
+            host_ws = torch.empty(op.host_workspace_bytes(shape, 64), dtype=torch.uint8, device=dev)
             e2e_step = lambda: op.forward_f16_host(shape, h_x, h_off, h_msk, packed, b16, h_out,  # noqa: E731
-                                                   chunk_images=64)
+                                                   chunk_images=64, workspace=host_ws)
         for _ in range(2):
             e2e_step()
         barrier(pg)
@@ -481,7 +542,10 @@ def run_ours(args):
                "h2d_bytes_per_step": (h_x.numel() + h_off.numel() + h_msk.numel()) * h_x.element_size(),
                "d2h_bytes_per_step": h_out.numel() * h_out.element_size() + (0 if cfg["f32"] else 4),
                "ms_per_step": e_ms, "steps": e_steps, "matches_device_resident_output": mism == 0,
-               "mismatched_outputs": mism, "per_rank_bytes": True}
+               "mismatched_outputs": mism, "per_rank_bytes": True,
+               "api": ("dcn_forward_f32 with pinned-host copies around it" if cfg["f32"] else
+                       "C ABI dcn_forward_f16_host: pinned host buffers in and out, chunks of 64 images "
+                       "pipelined inside the library (H2D, kernels, D2H overlapped), flag read back")}
         del h_x, h_off, h_msk, h_out
 
     # ---- CPU baseline (rank 0, one GPU only) ----------------------------------------
@@ -531,6 +595,7 @@ def run_ours(args):
                          "tensor_peak_source": f"{peak_kind} bf16_tflops (burst)",
                          "limiter": LIMITERS.get(kernel)},
             "cpu_baseline": cpu,
+            "parity": parity,
             "e2e": e2e,
             "raw_form": raw_form,
             "gather": gather,
@@ -560,6 +625,7 @@ def main():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--e2e-steps", type=int, default=5)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-parity", action="store_true", help="skip the oracle check of the timed output")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     args = ap.parse_args()
     if args.impl == "reference":

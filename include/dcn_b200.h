@@ -9,9 +9,10 @@
  *
  * Conventions
  *  - Plain C: pointers, sizes, one shape struct.  No CUDA, torch or C++ types.
- *  - All tensor pointers are DEVICE pointers owned by the caller.  Nothing is
- *    allocated per call; kernels that need scratch take a caller-provided
- *    workspace sized by the matching *_workspace_bytes() query.
+ *  - All tensor pointers are DEVICE pointers owned by the caller, except the
+ *    host buffers of dcn_forward_f16_host.  No device memory is allocated per
+ *    call; kernels that need scratch take a caller-provided workspace sized by
+ *    the matching *_workspace_bytes() query.
  *  - Every launch is asynchronous on the caller's stream (NULL = legacy default
  *    stream).  A status of DCN_OK means "validated and enqueued".  Errors that
  *    can only be seen on the device (non-finite output, a device-side pipeline
@@ -22,7 +23,8 @@
  *    mask [N][G*KH*KW][Ho][Wo], output NCHW.  FP32 weights are OIHW; packed
  *    weights are opaque (sized by dcn_packed_weight_bytes).
  *  - Thread safety: calls on distinct streams may run concurrently.  The only
- *    global state is a per-device attribute cache filled once under a mutex and
+ *    global state is a per-device attribute cache filled under a mutex (once per
+ *    device and CUDA context: a new context after cudaDeviceReset refills it) and
  *    the sticky device error word.
  */
 #ifndef DCN_B200_H
@@ -239,6 +241,30 @@ dcn_status dcn_forward_f16_grouped(const dcn_shape *shape, void *input_grouped,
                                    const void *bias, void *output, uint32_t *nonfinite_flag,
                                    dcn_stream stream);
 
+/* ---- FP16 operator on host buffers ----------------------------------------------
+ * Replaces the reference's host-array contract: MetalDeformConv.runFloat32 takes Swift
+ * arrays and returns a new array (MetalRunner.swift:159-185), copying the inputs into fresh
+ * shared buffers on every call (makeBuffer, :584-593).  Here input, offset, mask and output
+ * are HOST buffers in the layouts above (FP16); packed_weight and bias are device buffers as
+ * for dcn_forward_f16.  The batch is cut into chunks of `chunk_images` images (0: 64) and
+ * the chunks are pipelined on the library's own per-device streams -- up to three chunks in
+ * flight, each chunk's input copies (one cudaMemcpyAsync per tensor), dcn_forward_f16 and
+ * output copy in order on one stream -- so host->device copies, kernels and device->host
+ * copies overlap.  Host buffers should be page-locked (cudaHostAlloc / cudaHostRegister);
+ * pageable memory works but the copies then do not overlap.  `workspace` is device memory
+ * of dcn_forward_f16_host_workspace_bytes(shape, chunk_images) bytes (256-byte aligned):
+ * the staging buffers of the chunks in flight; the call allocates no device memory (its
+ * streams and events are created once per device and context).  The call is ordered after
+ * earlier work on `stream` and `stream` waits for all of it: once `stream` reaches that
+ * point, output_host holds the result and *nonfinite_flag_host (host memory, nullable) is
+ * DCN_FLAG_NONFINITE if any output is Inf/NaN, else 0.  Tensor-core-path shapes only (else
+ * DCN_ERR_UNSUPPORTED).  Concurrent calls on one device are enqueued one after another. */
+size_t dcn_forward_f16_host_workspace_bytes(const dcn_shape *shape, int32_t chunk_images);
+dcn_status dcn_forward_f16_host(const dcn_shape *shape, const void *input_host, const void *offset_host,
+                                const void *mask_host, const void *packed_weight, const void *bias,
+                                void *output_host, uint32_t *nonfinite_flag_host, int32_t chunk_images,
+                                void *workspace, size_t workspace_bytes, dcn_stream stream);
+
 /* ---- offset producer fused into the convolution ------------------------------------
  * prepare_dcn_offsets_fp16 (MetalShader.swift:817-839) followed by the DCN, as the
  * production graph chains them (FusedFourPassRecurrenceProbe.swift:609-630), in one
@@ -319,7 +345,9 @@ dcn_status dcn_prepare_offsets_f16(int64_t plane, const void *raw, const void *f
  * scratch exceeds the array returns DCN_ERR_SCRATCH_TOO_SMALL (16 MiB holds 15
  * Jasna 64x64 tiles on the slab path, 7 on the global-gather path).  All calls share the array, so calls that overlap on the GPU race
  * and must be ordered (one stream, or events).  The first call on a device looks
- * up the array's address; make it before any stream capture.  Allocates nothing. */
+ * up the array's address; make it before any stream capture (one warm-up call at
+ * start-up does it).  The address is kept per device and context and looked up
+ * again in a new context (after cudaDeviceReset).  Allocates nothing. */
 size_t dcn_static_scratch_bytes(void);
 dcn_status dcn_forward_f16_static_scratch(const dcn_shape *shape, const void *input,
                                           const void *offset, const void *mask,

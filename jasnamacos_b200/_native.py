@@ -139,6 +139,11 @@ PROTOTYPES = {
     "dcn_prepare_offsets_f16": (ctypes.c_int, [ctypes.c_int64, _P, _P, _P, _P, _P, _P]),
     "dcn_device_error": (ctypes.c_int, []),
     "dcn_check_wait_timeout": (ctypes.c_int, [ctypes.c_uint32, _P]),
+    "dcn_forward_f16_host_workspace_bytes": (ctypes.c_size_t, [_SHAPE, ctypes.c_int32]),
+    "dcn_forward_f16_host": (
+        ctypes.c_int,
+        [_SHAPE, _P, _P, _P, _P, _P, _P, _P, ctypes.c_int32, _P, ctypes.c_size_t, _P],
+    ),
     "dcn_static_scratch_bytes": (ctypes.c_size_t, []),
     "dcn_forward_f16_static_scratch": (ctypes.c_int, [_SHAPE, _P, _P, _P, _P, _P, _P, _P, _P]),
 }

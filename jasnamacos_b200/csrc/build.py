@@ -31,6 +31,7 @@ SOURCES = [
     "dcn_prepack.cu",
     "dcn_aux.cu",
     "dcn_static_scratch.cu",
+    "dcn_host.cu",
 ]
 HEADERS = ["dcn_common.cuh"]
 

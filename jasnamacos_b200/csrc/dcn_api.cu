@@ -6,6 +6,8 @@
 // return an error instead of the reference kernels' silent early return
 // (MetalShader.swift:192, :254-256).  Launches are asynchronous on the caller's
 // stream; nothing here allocates device memory.
+#include <cuda.h>
+#include <cudaTypedefs.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
@@ -62,15 +64,41 @@ cudaError_t launch_slab_grouped(const Params &p, const void *slabs, const __half
                                 const uint8_t *packed_w, const __half *bias, __half *output, uint32_t *flag,
                                 int sm_count, uint32_t *err, cudaStream_t stream);
 
+uint64_t current_context_id() {
+    static PFN_cuCtxGetCurrent_v4000 get_current = nullptr;
+    static PFN_cuCtxGetId_v12000 get_id = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void *a = nullptr, *b = nullptr;
+        cudaDriverEntryPointQueryResult qa, qb;
+        if (cudaGetDriverEntryPointByVersion("cuCtxGetCurrent", &a, 4000, cudaEnableDefault, &qa) == cudaSuccess &&
+            qa == cudaDriverEntryPointSuccess &&
+            cudaGetDriverEntryPointByVersion("cuCtxGetId", &b, 12000, cudaEnableDefault, &qb) == cudaSuccess &&
+            qb == cudaDriverEntryPointSuccess) {
+            get_current = reinterpret_cast<PFN_cuCtxGetCurrent_v4000>(a);
+            get_id = reinterpret_cast<PFN_cuCtxGetId_v12000>(b);
+        }
+        cudaGetLastError();
+    });
+    if (get_current == nullptr || get_id == nullptr) return 0;
+    CUcontext ctx = nullptr;
+    unsigned long long id = 0;
+    if (get_current(&ctx) != CUDA_SUCCESS || ctx == nullptr || get_id(ctx, &id) != CUDA_SUCCESS) return 0;
+    return id;
+}
+
 namespace {
 
 constexpr int kMaxDevices = 64;
 
+// Per device: the attributes every launch needs, filled with that device's context
+// current and valid for that context only (ctx_id).
 struct DeviceInfo {
     bool ready = false;
     bool sm100 = false;
     int sm_count = 0;
     uint32_t *err_word = nullptr;
+    uint64_t ctx_id = 0;
 };
 
 std::mutex g_mutex;
@@ -83,7 +111,10 @@ dcn_status from_cuda(cudaError_t e) {
     return DCN_ERR_LAUNCH;
 }
 
-// Looks up (once per device, under a mutex) the attributes every launch needs.
+// Looks up (once per device and context, under a mutex) the attributes every launch
+// needs.  A changed context id (cudaDeviceReset, then a new primary context) repeats
+// the set-up, since the error word's address and the kernels' shared-memory opt-in
+// belong to the old context.
 dcn_status current_device(DeviceInfo **out) {
     int dev = -1;
     cudaError_t e = cudaGetDevice(&dev);
@@ -94,7 +125,8 @@ dcn_status current_device(DeviceInfo **out) {
     if (dev < 0 || dev >= kMaxDevices) return DCN_ERR_NO_DEVICE;
     std::lock_guard<std::mutex> lock(g_mutex);
     DeviceInfo &d = g_devices[dev];
-    if (!d.ready) {
+    if (!d.ready || current_context_id() != d.ctx_id) {
+        d.ready = false;
         int major = 0, minor = 0, sms = 0;
         if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess ||
             cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev) != cudaSuccess ||
@@ -112,6 +144,7 @@ dcn_status current_device(DeviceInfo **out) {
                 return from_cuda(e);
             }
         }
+        d.ctx_id = current_context_id();
         d.ready = true;
     }
     if (!d.sm100) return DCN_ERR_UNSUPPORTED;  // the library carries sm_100a code only

@@ -66,6 +66,12 @@ struct SplitInput {
     }
 };
 
+// Unique id of the CUDA context current on the calling thread (cuCtxGetId), or 0 when
+// no context is current yet.  The per-device caches of device addresses and function
+// attributes record it and are rebuilt when it changes: after cudaDeviceReset the
+// runtime creates a new primary context, in which the old addresses are meaningless.
+uint64_t current_context_id();
+
 // Longest any device-side wait may spin before it gives up and reports
 // DCN_ERR_DEVICE_TIMEOUT (nanoseconds of %globaltimer).
 constexpr uint64_t kWaitLimitNs = 2000000000ull;

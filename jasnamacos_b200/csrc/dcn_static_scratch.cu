@@ -17,12 +17,16 @@
 //  * all calls share the one array: two calls that overlap on the GPU (different
 //    streams, no ordering between them) race on it and give wrong results;
 //  * the first call on a device looks up the array's device address
-//    (cudaGetSymbolAddress) -- make that first call before any stream capture.
+//    (cudaGetSymbolAddress) -- make that first call before any stream capture, for
+//    example as one warm-up call at start-up.  The address is kept per device
+//    together with the id of the context it belongs to; a call in a new context
+//    (after cudaDeviceReset) looks it up again.
 #include <cuda_runtime.h>
 
 #include <mutex>
 
 #include "dcn_b200.h"
+#include "dcn_common.cuh"
 
 namespace {
 
@@ -33,11 +37,16 @@ constexpr int kMaxDevices = 64;
 // symbol; the device address comes from cudaGetSymbolAddress below.
 static __device__ __align__(256) unsigned char g_static_scratch[kStaticScratchBytes];
 
-std::mutex g_scratch_mutex;
-void *g_scratch_address[kMaxDevices] = {};
+struct ScratchAddress {
+    void *ptr = nullptr;
+    uint64_t ctx_id = 0;  // context the address belongs to
+};
 
-// Device address of g_static_scratch on the current device, looked up once per
-// device with that device current.
+std::mutex g_scratch_mutex;
+ScratchAddress g_scratch_address[kMaxDevices];
+
+// Device address of g_static_scratch on the current device, looked up with that device
+// current once per device and context.
 dcn_status scratch_address(void **out) {
     int dev = -1;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) {
@@ -45,16 +54,19 @@ dcn_status scratch_address(void **out) {
         return DCN_ERR_NO_DEVICE;
     }
     std::lock_guard<std::mutex> lock(g_scratch_mutex);
-    if (g_scratch_address[dev] == nullptr) {
+    ScratchAddress &a = g_scratch_address[dev];
+    if (a.ptr == nullptr || dcn::current_context_id() != a.ctx_id) {
         void *ptr = nullptr;
         const cudaError_t e = cudaGetSymbolAddress(&ptr, g_static_scratch);
         if (e != cudaSuccess || ptr == nullptr) {
             cudaGetLastError();
+            a.ptr = nullptr;
             return e == cudaErrorNoKernelImageForDevice ? DCN_ERR_UNSUPPORTED : DCN_ERR_LAUNCH;
         }
-        g_scratch_address[dev] = ptr;
+        a.ptr = ptr;
+        a.ctx_id = dcn::current_context_id();
     }
-    *out = g_scratch_address[dev];
+    *out = a.ptr;
     return DCN_OK;
 }
 

@@ -478,60 +478,43 @@ class CudaDeformConv:
         """Raises DeviceTimeout if a kernel's bounded device-side wait expired since the last check."""
         raise_for_status(self.lib.dcn_device_error(), "device error word")
 
+    def host_workspace_bytes(self, shape: DeformConvShape, chunk_images: int = 0) -> int:
+        """Device staging memory of forward_f16_host (dcn_forward_f16_host_workspace_bytes)."""
+        return int(self.lib.dcn_forward_f16_host_workspace_bytes(ctypes.byref(shape.to_c()), chunk_images))
+
     def forward_f16_host(self, shape, input_host, offset_host, mask_host, packed_weight, bias, out_host,
-                         chunk_images: int | None = None, slots: int = 2):
-        """End-to-end FP16 operator on HOST buffers: the batch is cut into chunks of images and
-        each chunk's input/offset/mask are copied host->device, convolved by the fused kernel and
-        copied back, with `slots` chunks in flight on separate streams so copies in both
-        directions overlap the kernel.  Host tensors should be pinned (torch pin_memory) for
-        asynchronous copies.  Returns the non-finite flag (int) after synchronising; raises
-        NonFiniteOutput if it is set."""
+                         chunk_images: int = 0, workspace=None, stream=None, check: bool = True) -> int:
+        """End-to-end FP16 operator on HOST buffers through dcn_forward_f16_host: the library
+        cuts the batch into chunks of images and pipelines each chunk's host->device copies,
+        kernels and device->host copy on its own streams (up to three chunks in flight).  Host
+        tensors should be pinned (torch pin_memory) for the copies to overlap.  Synchronises
+        the stream, reads the non-finite flag (a 4-byte device->host copy inside the call) and
+        returns it; raises NonFiniteOutput if it is set and `check`."""
         torch = _torch()
         dev = packed_weight.device
-        n = shape.batch
-        if chunk_images is None:
-            chunk_images = max(1, min(n, 64))
-        chunk_images = max(1, min(chunk_images, n))
-        one = shape.with_batch(1)
-        per = (one.input_count, one.offset_count, one.mask_count, one.output_count)
-        cshape = shape.with_batch(chunk_images)
-        ws_bytes = self.workspace_bytes(cshape)
-        bufs = []
-        for _ in range(slots):
-            bufs.append({
-                "x": torch.empty(chunk_images * per[0], dtype=torch.float16, device=dev),
-                "off": torch.empty(chunk_images * per[1], dtype=torch.float16, device=dev),
-                "msk": torch.empty(chunk_images * per[2], dtype=torch.float16, device=dev),
-                "out": torch.empty(chunk_images * per[3], dtype=torch.float16, device=dev),
-                "ws": torch.empty(max(ws_bytes, 16), dtype=torch.uint8, device=dev),
-                "stream": torch.cuda.Stream(device=dev),
-                "done": None,
-            })
-        flag = torch.zeros(1, dtype=torch.int32, device=dev)
-        main = torch.cuda.current_stream(dev)
-        for ci, b0 in enumerate(range(0, n, chunk_images)):
-            b1 = min(n, b0 + chunk_images)
-            k = b1 - b0
-            slot = bufs[ci % slots]
-            st = slot["stream"]
-            st.wait_stream(main)
-            if slot["done"] is not None:
-                st.wait_event(slot["done"])
-            with torch.cuda.stream(st):
-                slot["x"][: k * per[0]].copy_(input_host[b0 * per[0]:b1 * per[0]], non_blocking=True)
-                slot["off"][: k * per[1]].copy_(offset_host[b0 * per[1]:b1 * per[1]], non_blocking=True)
-                slot["msk"][: k * per[2]].copy_(mask_host[b0 * per[2]:b1 * per[2]], non_blocking=True)
-                self.forward_f16(shape.with_batch(k), slot["x"][: k * per[0]], slot["off"][: k * per[1]],
-                                 slot["msk"][: k * per[2]], packed_weight, bias, out=slot["out"][: k * per[3]],
-                                 flag=flag, workspace=slot["ws"], stream=st)
-                out_host[b0 * per[3]:b1 * per[3]].copy_(slot["out"][: k * per[3]], non_blocking=True)
-                ev = torch.cuda.Event()
-                ev.record(st)
-                slot["done"] = ev
-        for slot in bufs:
-            main.wait_stream(slot["stream"])
-        value = int(flag.item())  # device -> host read of the step's result flag (synchronises)
-        if value & _native.DCN_FLAG_NONFINITE:
+        for name, arr, want in (("input", input_host, shape.input_count), ("offset", offset_host, shape.offset_count),
+                                ("mask", mask_host, shape.mask_count), ("output", out_host, shape.output_count)):
+            if arr.numel() != want:
+                raise InvalidArrayCount(name, want, arr.numel())
+            if arr.is_cuda or arr.dtype != torch.float16 or not arr.is_contiguous():
+                raise InvalidArgument(f"{name} must be a contiguous FP16 host tensor")
+        ws_bytes = self.host_workspace_bytes(shape, chunk_images)
+        if ws_bytes == 0:
+            raise Unsupported("shape does not take a tensor-core path")
+        if workspace is None:
+            workspace = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
+        self._check_device(packed_weight, bias, workspace)
+        flag_host = ctypes.c_uint32(0xFFFFFFFF)
+        s = stream if stream is not None else torch.cuda.current_stream(dev)
+        with torch.cuda.device(dev):
+            st = self.lib.dcn_forward_f16_host(
+                ctypes.byref(shape.to_c()), _ptr(input_host), _ptr(offset_host), _ptr(mask_host), _ptr(packed_weight),
+                _ptr(bias), _ptr(out_host), ctypes.addressof(flag_host), chunk_images, _ptr(workspace),
+                workspace.numel() * workspace.element_size(), s.cuda_stream or None)
+            raise_for_status(st, "dcn_forward_f16_host")
+            s.synchronize()
+        value = int(flag_host.value)
+        if check and value & _native.DCN_FLAG_NONFINITE:
             raise NonFiniteOutput("Inf/NaN in the DCNv2 output")
         return value
 

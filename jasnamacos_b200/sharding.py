@@ -51,3 +51,21 @@ def gather_to_root(local, total_tiles: int, per_tile: int, dist, root: int = 0, 
         for req in dist.batch_isend_irecv(ops):
             req.wait()
     return full
+
+
+def sample_tiles(total: int, ranges: int, per_range: int) -> list[int]:
+    """A deterministic parity sample: `per_range` tile indices spread evenly over each of the
+    `ranges` shard ranges of shard_range(total, r, ranges), first and last tile of every range
+    included (fewer when a range is shorter)."""
+    out: list[int] = []
+    for r in range(ranges):
+        b, e = shard_range(total, r, ranges)
+        n = e - b
+        if n <= 0:
+            continue
+        k = min(per_range, n)
+        if k == 1:
+            out.append(b)
+            continue
+        out.extend(sorted({b + (i * (n - 1)) // (k - 1) for i in range(k)}))
+    return out

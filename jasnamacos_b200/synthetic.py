@@ -11,7 +11,7 @@ its own documented rules:
 * normal: Box-Muller on two 53-bit uniforms, ``sqrt(-2 ln u1) * cos(2 pi u2)`` with
   ``u1`` in (0, 1].
 
-Configurations (shapes and distributions of the round's benchmark configs):
+Configurations (shapes and distributions of the DCNv2 benchmark set):
   0  FP32 1x128x64x64 -> 64, 3x3, pad 1, 16 deformable groups; x ~ N(0,1); W Kaiming-uniform
      U(+-1/sqrt(1152)); bias U(-0.1, 0.1); offset ~ N(0, 2^2); mask = sigmoid(N(0,1)).
   1  config 0 quantised to FP16.
@@ -228,3 +228,40 @@ def device_batch(shape: DeformConvShape, flow_range: float, seed: int, device, w
     msk = torch.sigmoid(torch.randn(n * pairs * plane, generator=g, device=device)).half()
     w, b = weights(shape, weight_seed)
     return x, off.reshape(-1), msk, w, b
+
+
+# Benchmark layout: which images a rank owns and how its inputs are seeded.  Tile batches
+# (configs 2 and 4) are sharded over the ranks; single-image configurations (0, 1, 3) run one
+# replica per rank.
+BENCH_SEED = 1000
+SHARDED_CONFIGS = (2, 4)
+FLOW_RANGE = {0: None, 1: None, 2: 16.0, 3: 32.0, 4: 16.0}
+
+
+def bench_images(config: int, rank: int, world: int, total_tiles: int | None = None) -> tuple[int, int]:
+    """Images [begin, end) of the benchmark batch that `rank` of `world` processes."""
+    from .sharding import shard_range
+
+    total = config_shape(config, total_tiles if config == 4 else None).batch
+    if config in SHARDED_CONFIGS:
+        return shard_range(total, rank, world)
+    return 0, total
+
+
+def bench_inputs(config: int, rank: int, world: int, device, total_tiles: int | None = None):
+    """The device-resident inputs the benchmark times for `config` on `rank` of `world`:
+    (shape of the rank's batch, first image index, x, offset, mask, weight, bias).  A rank's
+    batch is seeded with BENCH_SEED + its first image index, so any rank's data -- and with it
+    any tile of a benchmarked shard -- can be rebuilt on any GPU for parity checks."""
+    import torch
+
+    b, e = bench_images(config, rank, world, total_tiles)
+    shape = config_shape(config, batch=1).with_batch(e - b)
+    seed = BENCH_SEED + b
+    if config == 0:
+        data = device_gaussian_batch(shape, seed=seed, device=device, dtype=torch.float32)
+    elif FLOW_RANGE[config] is None:
+        data = device_gaussian_batch(shape, seed=seed, device=device)
+    else:
+        data = device_batch(shape, FLOW_RANGE[config], seed=seed, device=device)
+    return (shape, b) + tuple(data)

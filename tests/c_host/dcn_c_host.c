@@ -6,6 +6,9 @@
  *   - dcn_prepack_weights + dcn_forward_f16 on a slab-path batch (2 x 128 x 16 x 24, the
  *     group split with its reduction pass) and a global-gather image (1 x 128 x 64 x 96):
  *     FP16 gates max abs <= 2e-2, mean abs <= 2e-3;
+ *   - dcn_forward_f16_host on page-locked host buffers (5 images in chunks of 2, 2 and 1,
+ *     the chunks pipelined on the library's streams): FP16 gates against the oracle, and
+ *     the non-finite flag delivered to host memory;
  *   - dcn_forward_f32: bit-identical to the oracle;
  *   - the non-finite flag and the error codes of invalid shapes and misaligned pointers.
  * Inputs are multiples of powers of two small enough to be exact in FP16, so the FP16 and
@@ -216,6 +219,75 @@ static int check_f16(const dcn_shape *s, uint64_t seed, const char *name) {
     return (int)path;
 }
 
+/* The host-buffer entry point: inputs and output in page-locked host memory, chunks of
+ * `chunk` images pipelined by the library; FP16 gates against the oracle. */
+static void check_f16_host(const dcn_shape *s, uint64_t seed, int32_t chunk) {
+    case_data d = make_case(s, seed);
+    uint16_t *hx = NULL, *hoff = NULL, *hmsk = NULL, *hout = NULL;
+    uint32_t *hflag = NULL;
+    CUDA_OK(cudaHostAlloc((void **)&hx, sizeof(uint16_t) * (size_t)d.c.input, cudaHostAllocDefault));
+    CUDA_OK(cudaHostAlloc((void **)&hoff, sizeof(uint16_t) * (size_t)d.c.offset, cudaHostAllocDefault));
+    CUDA_OK(cudaHostAlloc((void **)&hmsk, sizeof(uint16_t) * (size_t)d.c.mask, cudaHostAllocDefault));
+    CUDA_OK(cudaHostAlloc((void **)&hout, sizeof(uint16_t) * (size_t)d.c.output, cudaHostAllocDefault));
+    CUDA_OK(cudaHostAlloc((void **)&hflag, sizeof(uint32_t), cudaHostAllocDefault));
+    for (int64_t i = 0; i < d.c.input; ++i) hx[i] = half_bits_exact(d.x[i]);
+    for (int64_t i = 0; i < d.c.offset; ++i) hoff[i] = half_bits_exact(d.off[i]);
+    for (int64_t i = 0; i < d.c.mask; ++i) hmsk[i] = half_bits_exact(d.msk[i]);
+    void *w = to_device_f16(d.w, d.c.weight), *b = to_device_f16(d.b, d.c.bias);
+    void *packed = NULL, *ws = NULL;
+    const size_t wsb = dcn_forward_f16_host_workspace_bytes(s, chunk);
+    CHECK(wsb > 0, "host workspace size");
+    CUDA_OK(cudaMalloc(&packed, dcn_packed_weight_bytes(s)));
+    CUDA_OK(cudaMalloc(&ws, wsb));
+    CHECK(dcn_prepack_weights(s, w, DCN_DTYPE_F16, DCN_WEIGHT_OIHW, packed, NULL) == DCN_OK, "host: prepack");
+    cudaStream_t stream;
+    CUDA_OK(cudaStreamCreate(&stream));
+    *hflag = 0xffffffffu;
+    dcn_status st = dcn_forward_f16_host(s, hx, hoff, hmsk, packed, b, hout, hflag, chunk, ws, wsb,
+                                         (dcn_stream)stream);
+    CHECK(st == DCN_OK, "dcn_forward_f16_host -> %s", dcn_status_string(st));
+    CUDA_OK(cudaStreamSynchronize(stream));
+    CHECK(*hflag == 0, "host: flag %u on finite output", *hflag);
+    CHECK(dcn_device_error() == DCN_OK, "host: device error word");
+    float *ref = oracle_run(s, &d);
+    double max_abs = 0.0, sum_abs = 0.0;
+    for (int64_t i = 0; i < d.c.output; ++i) {
+        const double e = fabs((double)half_to_float(hout[i]) - (double)ref[i]);
+        if (e > max_abs) max_abs = e;
+        sum_abs += e;
+    }
+    const double mean_abs = sum_abs / (double)d.c.output;
+    printf("host buffers, %d images in chunks of %d: FP16 max abs %.3g, mean abs %.3g\n", s->batch, chunk,
+           max_abs, mean_abs);
+    CHECK(max_abs <= 2e-2 && mean_abs <= 2e-3, "host: FP16 gates (max %.3g, mean %.3g)", max_abs, mean_abs);
+    CHECK(dcn_forward_f16_host(s, hx, hoff, hmsk, packed, b, hout, hflag, chunk, ws, wsb - 1, (dcn_stream)stream) ==
+              DCN_ERR_INVALID_ARGUMENT,
+          "host: short workspace accepted");
+
+    /* Infinite bias: every output non-finite, the flag must reach host memory. */
+    const uint16_t inf = 0x7c00u;
+    for (int64_t i = 0; i < d.c.bias; ++i) CUDA_OK(cudaMemcpy((uint16_t *)b + i, &inf, 2, cudaMemcpyHostToDevice));
+    *hflag = 0;
+    CHECK(dcn_forward_f16_host(s, hx, hoff, hmsk, packed, b, hout, hflag, chunk, ws, wsb, (dcn_stream)stream) ==
+              DCN_OK,
+          "host: overflow call");
+    CUDA_OK(cudaStreamSynchronize(stream));
+    CHECK(*hflag & DCN_FLAG_NONFINITE, "host: non-finite flag not delivered");
+
+    CUDA_OK(cudaStreamDestroy(stream));
+    free(ref);
+    cudaFreeHost(hx);
+    cudaFreeHost(hoff);
+    cudaFreeHost(hmsk);
+    cudaFreeHost(hout);
+    cudaFreeHost(hflag);
+    cudaFree(w);
+    cudaFree(b);
+    cudaFree(packed);
+    cudaFree(ws);
+    free_case(&d);
+}
+
 static void check_f32(const dcn_shape *s, uint64_t seed) {
     case_data d = make_case(s, seed);
     float *x = to_device_f32(d.x, d.c.input), *off = to_device_f32(d.off, d.c.offset);
@@ -271,6 +343,8 @@ int main(void) {
     const dcn_shape frame = jasna_shape(1, 64, 96);
     CHECK(check_f16(&slab, 11, "slab 2x16x24") == DCN_PATH_SLAB_TC, "slab shape took another path");
     CHECK(check_f16(&frame, 12, "global-gather 1x64x96") == DCN_PATH_FUSED_TC, "frame took another path");
+    const dcn_shape five = jasna_shape(5, 16, 24);
+    check_f16_host(&five, 14, 2);
     check_f32(&slab, 13);
     check_errors();
     if (failures) {

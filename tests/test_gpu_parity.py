@@ -1,7 +1,7 @@
 """GPU parity against the CPU oracle (the restatement of DeformConvCPU.run,
 Sources/JasnaMetalPoC/DeformConv.swift:75-166), every call through the C ABI.
 
-Gates (the round's north star):
+Gates (the operator's numerical contract):
   * FP32 path: bit-identical to the oracle (which implies max relative error <= 1e-5,
     denominator max(|ref|, 1e-6) as JasnaCLI.swift:105).
   * FP16 path: max abs <= 2e-2 and mean abs <= 2e-3 against the FP32 oracle run on the

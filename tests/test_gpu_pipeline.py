@@ -1,6 +1,7 @@
-"""GPU: the host-buffer pipeline (forward_f16_host: chunks of images copied in, convolved and
-copied out on two streams) returns exactly what the device-resident operator returns, and
-large batches are deterministic run to run with no device-side timeout recorded."""
+"""GPU: the host-buffer pipeline (dcn_forward_f16_host through forward_f16_host: chunks of
+images copied in, convolved and copied out on the library's own streams) returns exactly what
+the device-resident operator returns, and large batches are deterministic run to run with no
+device-side timeout recorded."""
 
 from __future__ import annotations
 

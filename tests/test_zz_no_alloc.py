@@ -1,8 +1,12 @@
 """GPU: dcn_forward_f16_static_scratch, the entry point for callers that cannot allocate
 device memory when they run the convolution (its scratch lives in a fixed 16 MiB array
 inside the library), called through the C ABI and compared with dcn_forward_f16 given a
-caller workspace, on two calls in a row with different inputs.  Collected last on purpose
-(file name), and self-contained, so it passes alone in a fresh process or after the rest."""
+caller workspace, on two calls in a row with different inputs.  Both entry points run the
+same kernels on the same inputs in the same order, so the outputs must be identical bit for
+bit; the first call's output is also checked against the CPU oracle, the device's free
+memory must not change across the second call, and the sticky device error word must stay
+clear.  Collected last on purpose (file name), and self-contained, so it passes alone in a
+fresh process or after the rest."""
 
 from __future__ import annotations
 
@@ -30,6 +34,8 @@ def test_static_scratch_matches_workspace_entry_point_twice(batch):
     SMs with their FP32 partial sums kept in the static scratch too."""
     import torch
 
+    import oracle
+
     assert torch.cuda.is_available()
     lib = _native.load()
     shape = DeformConvShape.jasna_propagation(batch=batch)
@@ -45,22 +51,41 @@ def test_static_scratch_matches_workspace_entry_point_twice(batch):
     assert ws_bytes <= lib.dcn_static_scratch_bytes()
     ws = torch.empty(ws_bytes, dtype=torch.uint8, device="cuda")
 
-    for call, seed in enumerate((31, 32)):  # two calls in a row, different inputs
+    # Everything both calls need is allocated before the first call, so that the free-memory
+    # reading around the second call sees only what the entry point itself might allocate.
+    calls = []
+    for seed in (31, 32):  # two calls in a row, different inputs
         x, off, msk, _, _ = synthetic.device_batch(shape, 16.0, seed=seed, device="cuda")
-        ref = torch.empty(shape.output_count, dtype=torch.float16, device="cuda")
-        out = torch.full((shape.output_count,), float("nan"), dtype=torch.float16, device="cuda")
-        flag = torch.zeros(1, dtype=torch.int32, device="cuda")
-        st = lib.dcn_forward_f16(ctypes.byref(c_shape), _p(x), _p(off), _p(msk), _p(packed), _p(b16), _p(ref),
-                                 None, _p(ws), ws_bytes, None)
+        calls.append(dict(x=x, off=off, msk=msk,
+                          ref=torch.empty(shape.output_count, dtype=torch.float16, device="cuda"),
+                          out=torch.full((shape.output_count,), float("nan"), dtype=torch.float16, device="cuda"),
+                          flag=torch.zeros(1, dtype=torch.int32, device="cuda")))
+    torch.cuda.synchronize()
+    for call, c in enumerate(calls):
+        st = lib.dcn_forward_f16(ctypes.byref(c_shape), _p(c["x"]), _p(c["off"]), _p(c["msk"]), _p(packed),
+                                 _p(b16), _p(c["ref"]), None, _p(ws), ws_bytes, None)
         assert st == _native.DCN_OK
-        st = lib.dcn_forward_f16_static_scratch(ctypes.byref(c_shape), _p(x), _p(off), _p(msk), _p(packed),
-                                                _p(b16), _p(out), _p(flag), None)
+        torch.cuda.synchronize()
+        free_before = torch.cuda.mem_get_info()[0]
+        st = lib.dcn_forward_f16_static_scratch(ctypes.byref(c_shape), _p(c["x"]), _p(c["off"]), _p(c["msk"]),
+                                                _p(packed), _p(b16), _p(c["out"]), _p(c["flag"]), None)
         assert st == _native.DCN_OK, _native.status_string(st)
         torch.cuda.synchronize()
-        assert int(flag.item()) == 0
-        d = (out.float() - ref.float()).abs().cpu().numpy()
-        assert np.isfinite(d).all(), f"call {call}: non-finite output"
-        assert float(d.max()) <= F16_MAX_ABS and float(d.mean()) <= F16_MEAN_ABS, (call, float(d.max()))
+        free_after = torch.cuda.mem_get_info()[0]
+        if call == 1:  # the first call on a device may load the library's module (the array itself)
+            assert free_after == free_before, (free_before, free_after)
+        assert int(c["flag"].item()) == 0
+        assert torch.equal(c["out"], c["ref"]), f"call {call}: static-scratch output differs from dcn_forward_f16"
+    assert lib.dcn_device_error() == _native.DCN_OK
+
+    # One oracle check (first call): the shared output is also right, not just repeatable.
+    c = calls[0]
+    ref = oracle.run(shape, c["x"].float().cpu().numpy(), c["off"].float().cpu().numpy(),
+                     c["msk"].float().cpu().numpy(), w16.float().cpu().numpy(), b16.float().cpu().numpy(),
+                     threads=oracle.host_threads())
+    d = np.abs(c["out"].float().cpu().numpy() - ref)
+    assert np.isfinite(d).all()
+    assert float(d.max()) <= F16_MAX_ABS and float(d.mean()) <= F16_MEAN_ABS, (float(d.max()), float(d.mean()))
 
 
 def test_static_scratch_rejects_problems_beyond_its_size():
