@@ -451,6 +451,7 @@ def run_ours(args):
         kernel_ms = ms / args.steps
         launches_per_step = 1 if cfg["f32"] else 2
     torch.cuda.synchronize(dev)
+    kernel_ms_max = max_over_ranks(kernel_ms, pg)  # every rank takes this collective
     bytes_per_px = BYTES_PER_PX * (2 if cfg["f32"] else 1)
     achieved_gbs = bytes_per_px * px_per_step / (kernel_ms * 1e-3) / 1e9
     tensor_tflops = FLOPS_PER_PX * px_per_step / (kernel_ms * 1e-3) / 1e12
@@ -476,26 +477,63 @@ def run_ours(args):
                             "computed inside the kernel (prepare_dcn_offsets_fp16 fused)"}
         del raw, f1, f2, wsr
 
-    # ---- final gather of every shard's output to rank 0 (N > 1, after the timed step) ---
+    # ---- final gather of every shard's output to rank 0 (N > 1) -------------------------
+    # (a) serial: the timed step's output sent after the step; (b) overlapped: the shard
+    # computed in chunks, each finished chunk sent to rank 0 while the next one is computed.
     gather = None
-    if pg is not None and cfg["sharded"]:
+    if pg is not None and cfg["sharded"] and not cfg["f32"]:
         from jasnamacos_b200 import sharding
 
         per_image = base_shape.output_count
         full = torch.empty(total_images * per_image, dtype=out.dtype, device=dev) if rank == 0 else None
-        gather_step = lambda: sharding.gather_to_root(out, total_images, per_image, pg, out=full)  # noqa: E731
-        gather_step()  # connection set-up, untimed
+        g_iters = 20
+        serial = lambda: sharding.gather_to_root(out, total_images, per_image, pg, out=full)  # noqa: E731
+        serial()  # connection set-up, untimed
         torch.cuda.synchronize(dev)
         barrier(pg)
-        g_ms = max_over_ranks(event_time_ms(gather_step, 3), pg) / 3
+        g_local = event_time_ms(serial, g_iters) / g_iters
+        torch.cuda.synchronize(dev)
+        g_ms = max_over_ranks(g_local, pg)
+        root_ms = max_over_ranks(g_local if rank == 0 else 0.0, pg)
+        serial_full = full.clone() if rank == 0 else None
         own = (i_end - i_begin) if rank == 0 else 0
         recv_bytes = (total_images - own) * per_image * out.element_size() if rank == 0 else 0
         recv_bytes = int(max_over_ranks(float(recv_bytes), pg))
-        gather = {"ms": g_ms, "bytes_to_root": recv_bytes, "GB_s": recv_bytes / (g_ms * 1e-3) / 1e9,
-                  "value_with_gather": job_px / ((ms_per_step + g_ms) * 1e-3) / 1e6, "unit": "Mpx/s",
-                  "what": "every rank's output shard to rank 0 (NCCL point-to-point, receives posted together); "
-                          "not part of the timed step"}
-        del full
+        one = base_shape.with_batch(1)
+        pin_, poff, pmsk = one.input_count, one.offset_count, one.mask_count
+
+        def compute(cb, ce, dst):
+            lb, le = cb - i_begin, ce - i_begin
+            op.forward_f16(one.with_batch(ce - cb), x[lb * pin_:le * pin_], off[lb * poff:le * poff],
+                           msk[lb * pmsk:le * pmsk], packed, b16, out=dst, flag=flag, workspace=ws)
+
+        def overlapped():
+            for wk in sharding.compute_and_gather(compute, total_images, per_image, pg,
+                                                  local=out if rank != 0 else None, full=full,
+                                                  chunks=args.gather_chunks):
+                wk.wait()
+
+        for _ in range(3):
+            overlapped()
+        torch.cuda.synchronize(dev)
+        barrier(pg)
+        o_ms = max_over_ranks(event_time_ms(overlapped, g_iters) / g_iters, pg)
+        torch.cuda.synchronize(dev)
+        same = bool(torch.equal(full, serial_full)) if rank == 0 else True
+        same = max_over_ranks(0.0 if same else 1.0, pg) == 0.0
+        gather = {"serial": {"ms": g_ms, "root_ms": root_ms, "GB_s": recv_bytes / (g_ms * 1e-3) / 1e9,
+                             "value_with_gather": job_px / ((ms_per_step + g_ms) * 1e-3) / 1e6,
+                             "what": "the timed step's output shards to rank 0 after the step (NCCL point-to-point, "
+                                     "receives posted together), max over ranks of 20 CUDA-event-timed iterations"},
+                  "overlapped": {"ms_per_step": o_ms, "chunks": args.gather_chunks,
+                                 "value_with_gather": job_px / (o_ms * 1e-3) / 1e6,
+                                 "what": "each rank computes its shard in chunks (dcn_forward_f16 per chunk) and sends "
+                                         "every finished chunk to rank 0 while the next is computed; rank 0 computes "
+                                         "into the gathered tensor; step ends when rank 0 holds every output",
+                                 "output_equals_serial_gather": same},
+                  "bytes_to_root": recv_bytes, "unit": "Mpx/s",
+                  "value_with_gather": job_px / (o_ms * 1e-3) / 1e6}
+        del full, serial_full
         torch.cuda.synchronize(dev)
         barrier(pg)
 
@@ -594,6 +632,11 @@ def run_ours(args):
                          "tensor_frac": tensor_tflops / peaks["bf16_tflops"] if tensor_path else None,
                          "tensor_peak_source": f"{peak_kind} bf16_tflops (burst)",
                          "limiter": LIMITERS.get(kernel)},
+            "grouped_input_form": ({"value": job_px / (kernel_ms_max * 1e-3) / 1e6, "unit": "Mpx/s",
+                                    "ms_per_step": kernel_ms_max,
+                                    "what": "dcn_forward_f16_grouped on an input already in the path's grouped layout "
+                                            "(a producer that writes that layout itself skips the regroup pre-pass)"}
+                                   if tensor_path else None),
             "cpu_baseline": cpu,
             "parity": parity,
             "e2e": e2e,
@@ -622,6 +665,8 @@ def main():
     ap.add_argument("--no-raw", action="store_true", help="skip the fused offset-producer measurement")
     ap.add_argument("--graph", choices=("auto", "on", "off"), default="auto",
                     help="time steps as CUDA graph replays (auto: for the single-image configs 0, 1, 3)")
+    ap.add_argument("--gather-chunks", type=int, default=4,
+                    help="N > 1: chunks per shard in the overlapped compute + gather pass")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--e2e-steps", type=int, default=5)
     ap.add_argument("--no-cpu-baseline", action="store_true")

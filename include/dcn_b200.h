@@ -221,9 +221,16 @@ dcn_status dcn_forward_f16(const dcn_shape *shape, const void *input, const void
 /* The two launches dcn_forward_f16 makes, for callers that keep their features
  * channels-last and for timing the tensor-core kernel alone.
  * dcn_regroup_input_f16: NCHW FP16 input -> the grouped channels-last layout of the
- *   selected path in `workspace` (dcn_forward_f16_workspace_bytes bytes): 8 channels
- *   of one deformable group per 16 bytes, as zero-bordered per-group slabs
- *   (DCN_PATH_SLAB_TC) or as 32-byte horizontal corner pairs (DCN_PATH_FUSED_TC).
+ *   selected path at the start of `workspace` (dcn_forward_f16_workspace_bytes bytes),
+ *   8 channels of one deformable group per 16 bytes:
+ *     DCN_PATH_SLAB_TC  zero-bordered per-group slabs [N][C/8][H+2][W+2][8] FP16, element
+ *                       (n, g, y+1, x+1, c) = input[n][8g+c][y][x], the one-pixel ring zero;
+ *     DCN_PATH_FUSED_TC horizontal corner pairs [N][C/8][H][W+1] of 32 bytes: entry
+ *                       (n, g, y, x) = the 8 channels at column x-1, then at column x
+ *                       (zeros outside the image).
+ *   A producer that writes its features in this layout itself (the reference assembles
+ *   the DCN input in its own kernel, MetalShader.swift:769-813) can skip the pre-pass and
+ *   call dcn_forward_f16_grouped directly.
  * dcn_forward_f16_grouped: the tensor-core kernel reading such an input from the
  *   start of a workspace (16-byte aligned, dcn_forward_f16_workspace_bytes bytes): on
  *   the slab path, batches with fewer 128-pixel tiles than the B200 has SMs split the

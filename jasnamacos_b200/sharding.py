@@ -69,3 +69,45 @@ def sample_tiles(total: int, ranges: int, per_range: int) -> list[int]:
             continue
         out.extend(sorted({b + (i * (n - 1)) // (k - 1) for i in range(k)}))
     return out
+
+
+def chunk_ranges(begin: int, end: int, chunks: int) -> list[tuple[int, int]]:
+    """`chunks` consecutive ranges covering [begin, end) (sizes differ by at most one; empty
+    ranges allowed), the same split rule on every rank."""
+    n = end - begin
+    return [(begin + n * k // chunks, begin + n * (k + 1) // chunks) for k in range(chunks)]
+
+
+def compute_and_gather(compute, total_tiles: int, per_tile: int, dist, local=None, full=None, root: int = 0,
+                       chunks: int = 4):
+    """One pass over this rank's tile shard with the gather to `root` overlapped: the shard is
+    cut into `chunks` consecutive chunks (chunk_ranges, the same rule on every rank); after
+    `compute(b, e, dst)` has enqueued chunk [b, e) (global tile indices) on the current
+    stream, writing its output into `dst`, the chunk goes to `root` over NCCL point-to-point
+    while the next chunk is computed.  NCCL's stream waits only for the work enqueued before
+    the send, so the transfer of chunk k overlaps the kernels of chunk k+1.
+
+    `local` (non-root ranks) is the rank's [shard * per_tile] output tensor; `full` (root) the
+    [total_tiles * per_tile] tensor that receives every shard -- root computes its own chunks
+    straight into it.  Returns the list of NCCL work handles; the caller waits on them
+    (work.wait() orders the current stream after the transfers).  Every rank takes the same
+    steps in the same order."""
+    rank, world = dist.get_rank(), dist.get_world_size()
+    b, e = shard_range(total_tiles, rank, world)
+    mine = chunk_ranges(b, e, chunks)
+    peers = {src: chunk_ranges(*shard_range(total_tiles, src, world), chunks) for src in range(world) if src != root}
+    works = []
+    for k, (cb, ce) in enumerate(mine):
+        if rank == root:
+            if ce > cb:
+                compute(cb, ce, full[cb * per_tile:ce * per_tile])
+            ops = [dist.P2POp(dist.irecv, full[pb * per_tile:pe * per_tile], src)
+                   for src, ranges in peers.items() for pb, pe in [ranges[k]] if pe > pb]
+        else:
+            dst = local[(cb - b) * per_tile:(ce - b) * per_tile]
+            if ce > cb:
+                compute(cb, ce, dst)
+            ops = [dist.P2POp(dist.isend, dst, root)] if ce > cb else []
+        if ops:
+            works.extend(dist.batch_isend_irecv(ops))
+    return works

@@ -35,14 +35,14 @@ def _free_port() -> int:
         return s.getsockname()[1]
 
 
-def _worker(rank, world, port, total, per_tile, fail_rank, q):
+def _worker(rank, world, port, total, per_tile, fail_rank, q, mode="gather", chunks=3):
     sys.path.insert(0, str(REPO))
     import datetime
 
     import torch
     import torch.distributed as dist
 
-    from jasnamacos_b200.sharding import gather_to_root, shard_range
+    from jasnamacos_b200.sharding import compute_and_gather, gather_to_root, shard_range
 
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=10))
@@ -51,7 +51,23 @@ def _worker(rank, world, port, total, per_tile, fail_rank, q):
         local = torch.arange(b * per_tile, e * per_tile, dtype=torch.float32)  # "output" of my tiles
         if rank == fail_rank:
             raise RuntimeError("injected host-side failure before the gather")
-        full = gather_to_root(local, total, per_tile, dist)
+        if mode == "gather":
+            full = gather_to_root(local, total, per_tile, dist)
+        else:  # chunks computed into place and sent to rank 0 as they finish
+            computed = []
+
+            def compute(cb, ce, dst):
+                computed.append((cb, ce))
+                dst.copy_(torch.arange(cb * per_tile, ce * per_tile, dtype=torch.float32))
+
+            full = torch.full((total * per_tile,), -1.0) if rank == 0 else None
+            mine = torch.empty((e - b) * per_tile) if rank != 0 else None
+            for w in compute_and_gather(compute, total, per_tile, dist, local=mine, full=full, chunks=chunks):
+                w.wait()
+            assert sum(ce - cb for cb, ce in computed) == e - b
+            if rank != 0:
+                assert torch.equal(mine, local)
+                full = None
         if rank == 0:
             q.put(("ok", bool(torch.equal(full, torch.arange(total * per_tile, dtype=torch.float32)))))
         else:
@@ -65,13 +81,14 @@ def _worker(rank, world, port, total, per_tile, fail_rank, q):
             pass
 
 
-def _run(world, total, per_tile, fail_rank=-1, timeout=60):
+def _run(world, total, per_tile, fail_rank=-1, timeout=60, mode="gather", chunks=3):
     import multiprocessing as mp
 
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, total, per_tile, fail_rank, q)) for r in range(world)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, total, per_tile, fail_rank, q, mode, chunks))
+             for r in range(world)]
     for p in procs:
         p.start()
     results = []
@@ -94,3 +111,11 @@ def test_failed_rank_surfaces_as_error_not_hang():
     results = _run(2, 8, per_tile=3, fail_rank=1, timeout=90)
     kinds = sorted(kind for kind, _ in results)
     assert kinds == ["error", "error"], results  # rank 1 failed; rank 0's recv timed out or was aborted
+
+
+@pytest.mark.parametrize("world,total,chunks", [(2, 7, 3), (3, 16, 4), (3, 2, 4)])
+def test_compute_and_gather_gloo(world, total, chunks):
+    """The overlapped pass: every rank computes its shard chunk by chunk and each finished
+    chunk is sent to rank 0 (some chunks empty when a shard is shorter than the chunk count)."""
+    results = _run(world, total, per_tile=5, mode="pipelined", chunks=chunks)
+    assert all(kind == "ok" and flag for kind, flag in results), results
