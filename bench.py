@@ -521,6 +521,46 @@ def run_ours(args):
         torch.cuda.synchronize(dev)
         same = bool(torch.equal(full, serial_full)) if rank == 0 else True
         same = max_over_ranks(0.0 if same else 1.0, pg) == 0.0
+        # (c) overlapped with copy-engine peer copies into rank 0's tensor (CUDA IPC)
+        peer_line = None
+        try:
+            peer = sharding.PeerGather(full, total_images, per_image, pg)
+        except Exception as exc:  # noqa: BLE001 - reported in the line; every rank takes the same path
+            peer, peer_line = None, {"unavailable": f"{type(exc).__name__}: {exc}"[:200]}
+        ok_all = max_over_ranks(0.0 if peer is not None else 1.0, pg) == 0.0
+        if ok_all:
+            if rank == 0:
+                full.zero_()
+            torch.cuda.synchronize(dev)
+            barrier(pg)
+            copy_stream = torch.cuda.Stream(device=dev)
+
+            def overlapped_peer():
+                sharding.compute_and_copy_to_root(compute, total_images, per_image, pg, peer,
+                                                  local=out if rank != 0 else None, full=full,
+                                                  chunks=args.gather_chunks, copy_stream=copy_stream)
+
+            for _ in range(3):
+                overlapped_peer()
+            torch.cuda.synchronize(dev)
+            barrier(pg)
+            p_ms = max_over_ranks(event_time_ms(overlapped_peer, g_iters) / g_iters, pg)
+            torch.cuda.synchronize(dev)
+            barrier(pg)  # every peer copy has landed before rank 0 compares
+            psame = bool(torch.equal(full, serial_full)) if rank == 0 else True
+            psame = max_over_ranks(0.0 if psame else 1.0, pg) == 0.0
+            peer.close()
+            barrier(pg)
+            peer_line = {"ms_per_step": p_ms, "chunks": args.gather_chunks,
+                         "value_with_gather": job_px / (p_ms * 1e-3) / 1e6,
+                         "what": "as overlapped, but each finished chunk is copied into rank 0's tensor by the "
+                                 "copy engines (cudaMemcpyAsync peer copy over NVLink through a CUDA IPC "
+                                 "mapping) on a side stream: no kernel, no SM time for the transfer",
+                         "output_equals_serial_gather": psame}
+        else:
+            if peer is not None:
+                peer.close()
+            barrier(pg)
         gather = {"serial": {"ms": g_ms, "root_ms": root_ms, "GB_s": recv_bytes / (g_ms * 1e-3) / 1e9,
                              "value_with_gather": job_px / ((ms_per_step + g_ms) * 1e-3) / 1e6,
                              "what": "the timed step's output shards to rank 0 after the step (NCCL point-to-point, "
@@ -531,8 +571,12 @@ def run_ours(args):
                                          "every finished chunk to rank 0 while the next is computed; rank 0 computes "
                                          "into the gathered tensor; step ends when rank 0 holds every output",
                                  "output_equals_serial_gather": same},
-                  "bytes_to_root": recv_bytes, "unit": "Mpx/s",
-                  "value_with_gather": job_px / (o_ms * 1e-3) / 1e6}
+                  "peer_copy": peer_line,
+                  "bytes_to_root": recv_bytes, "unit": "Mpx/s"}
+        best = [gather["overlapped"]["value_with_gather"]]
+        if peer_line and "value_with_gather" in peer_line and peer_line["output_equals_serial_gather"]:
+            best.append(peer_line["value_with_gather"])
+        gather["value_with_gather"] = max(best)
         del full, serial_full
         torch.cuda.synchronize(dev)
         barrier(pg)

@@ -309,6 +309,32 @@ __device__ __forceinline__ void tmem_st_32x32b_x4(uint32_t taddr, uint32_t r0, u
                  : "memory");
 }
 
+// 32 lanes x 16 consecutive 32-bit columns from v[0..15], then tcgen05.wait::st, in one asm
+// statement.  The source registers are operands of the statement that also waits, so the
+// compiler cannot give them to other values while the store may still be reading them (a
+// separate asm statement for the wait would allow that).
+__device__ __forceinline__ void tmem_st_32x32b_x16_wait(uint32_t taddr, const uint32_t (&v)[16]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+        "{%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16};\n\t"
+        "tcgen05.wait::st.sync.aligned;" ::"r"(taddr),
+        "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]),
+        "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
+        : "memory");
+}
+
+// 12 consecutive 32-bit columns (an x8 and an x4 store) from v, then tcgen05.wait::st, in one
+// asm statement (same reason as above).
+__device__ __forceinline__ void tmem_st_32x32b_x12_wait(uint32_t taddr, const uint32_t (&v)[3][4]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};\n\t"
+        "tcgen05.st.sync.aligned.32x32b.x4.b32 [%9], {%10, %11, %12, %13};\n\t"
+        "tcgen05.wait::st.sync.aligned;" ::"r"(taddr),
+        "r"(v[0][0]), "r"(v[0][1]), "r"(v[0][2]), "r"(v[0][3]), "r"(v[1][0]), "r"(v[1][1]), "r"(v[1][2]),
+        "r"(v[1][3]), "r"(taddr + 8), "r"(v[2][0]), "r"(v[2][1]), "r"(v[2][2]), "r"(v[2][3])
+        : "memory");
+}
+
 // 32 lanes x 16 consecutive 32-bit columns into v[0..15].
 __device__ __forceinline__ void tmem_ld_32x32b_x16(uint32_t taddr, uint32_t *v) {
     asm volatile(

@@ -392,7 +392,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         auto commit = [&](uint32_t itc, StageRegs &R) -> bool {
             const uint32_t st = itc % kStages;
             const uint32_t ph = (itc / kStages) & 1u;
-            uint32_t outw[4][4];
+            uint32_t outw[16];  // 4 chunks x 4 columns
 #pragma unroll
             for (int c4 = 0; c4 < 4; ++c4) {
                 const float2 f = __half22float2(*reinterpret_cast<const __half2 *>(&R.frac[c4]));
@@ -410,18 +410,13 @@ __global__ void __launch_bounds__(kThreads, 1)
                     acc = __hfma2(w01, h[4 + e], acc);
                     acc = __hfma2(w10, h[8 + e], acc);
                     acc = __hfma2(w11, h[12 + e], acc);
-                    outw[c4][e] = pack_half2(acc);
+                    outw[c4 * 4 + e] = pack_half2(acc);
                 }
             }
             if (!mbar_wait_bounded(&s.a_empty[st], ph ^ 1u, abort_flag)) return false;
             tc_fence_after();
-#pragma unroll
-            for (int c4 = 0; c4 < 4; ++c4) {
-                const int c = half_sel * 4 + c4;
-                tmem_st_32x32b_x4(lane_base + kACol0 + st * kAStageCols + c * 4, outw[c4][0], outw[c4][1],
-                                  outw[c4][2], outw[c4][3]);
-            }
-            tmem_wait_st();
+            // Chunks half_sel*4 .. half_sel*4+3 are 16 consecutive columns.
+            tmem_st_32x32b_x16_wait(lane_base + kACol0 + st * kAStageCols + half_sel * 16, outw);
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&s.a_full[st]);

@@ -280,7 +280,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (lane == 0) {
             const uint32_t idesc = make_idesc_f16_f32(BM, BN);
             uint32_t gi = 0, si = 0;
-            uint32_t uses[kMaxTilesPerUnit] = {0, 0, 0, 0};
+            uint32_t acc_par = 0;  // bit t: parity of tile t's current accumulator phase (a register, not an array)
             uint64_t *last_bar = nullptr;
             uint32_t last_parity = 0;
             bool ok = true;
@@ -297,7 +297,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     const uint32_t b_base = smem_addr(s.b[gb]);
                     for (int t = 0; t < mt; ++t, ++si) {
                         if (g == w.g0) {
-                            if (!mbar_wait_bounded(&s.acc_empty[t], (uses[t] & 1u) ^ 1u, abort_flag)) {
+                            if (!mbar_wait_bounded(&s.acc_empty[t], ((acc_par >> t) & 1u) ^ 1u, abort_flag)) {
                                 signal_abort(s, a.err);
                                 ok = false;
                                 break;
@@ -323,8 +323,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                         if (g == g_last) {
                             umma_commit(&s.acc_full[t]);
                             last_bar = &s.acc_full[t];
-                            last_parity = uses[t] & 1u;
-                            ++uses[t];
+                            last_parity = (acc_par >> t) & 1u;
+                            acc_par ^= 1u << t;
                         }
                     }
                     if (!ok) break;
@@ -339,19 +339,19 @@ __global__ void __launch_bounds__(kThreads, 1)
         // ---------------------------------------------------------- epilogue
         const int q = warp % 4;
         const int r = q * 32 + lane;
-        uint32_t uses[kMaxTilesPerUnit] = {0, 0, 0, 0};
+        uint32_t acc_par = 0;  // bit t: parity of tile t's next acc_full phase
         bool nonfinite = false;
         bool ok = true;
         for (int u = blockIdx.x; u < a.num_units && ok; u += gridDim.x) {
             const Unit w = decode_unit(a, u);
             const int n = w.n, t0 = w.t0, mt = w.mt;
             for (int t = 0; t < mt; ++t) {
-                if (!mbar_wait_bounded(&s.acc_full[t], uses[t] & 1u, abort_flag, kIdleBackoffNs)) {
+                if (!mbar_wait_bounded(&s.acc_full[t], (acc_par >> t) & 1u, abort_flag, kIdleBackoffNs)) {
                     signal_abort(s, a.err);
                     ok = false;
                     break;
                 }
-                ++uses[t];
+                acc_par ^= 1u << t;
                 tc_fence_after();
                 uint32_t v[BN];
                 const uint32_t taddr = tmem + (static_cast<uint32_t>(q * 32) << 16) + t * BN;
@@ -376,10 +376,15 @@ __global__ void __launch_bounds__(kThreads, 1)
                 } else if (px < p.out_plane) {
                     __half *dst = a.out + output_index(p, n, 0, px);
 #pragma unroll
-                    for (int oc = 0; oc < BN; ++oc) {
-                        const __half h = __float2half_rn(__uint_as_float(v[oc]) + s.bias[oc]);
-                        nonfinite |= __hisinf(h) != 0 || __hisnan(h);
-                        dst[static_cast<size_t>(oc) * p.out_plane] = h;
+                    for (int oc = 0; oc < BN; oc += 4) {
+                        const float4 bq = *reinterpret_cast<const float4 *>(&s.bias[oc]);
+                        const float bb[4] = {bq.x, bq.y, bq.z, bq.w};
+#pragma unroll
+                        for (int j = 0; j < 4; ++j) {
+                            const __half h = __float2half_rn(__uint_as_float(v[oc + j]) + bb[j]);
+                            nonfinite |= __hisinf(h) != 0 || __hisnan(h);
+                            dst[static_cast<size_t>(oc + j) * p.out_plane] = h;
+                        }
                     }
                 }
             }
@@ -396,14 +401,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int sw = p.W + 2;  // slab row stride in positions
         const uint32_t slab0 = smem_addr(slab_base);
         // This warp's taps as float offsets (ky*DH, kx*DW): integer-valued, so adding
-        // them to the pixel's integer base in FP32 is exact, as in the reference.
-        float tyf[3], txf[3];
+        // them to the pixel's integer base in FP32 is exact, as in the reference.  The slab
+        // kernel takes 3x3 kernels only, so the warp's three taps tap0..tap0+2 are one kernel
+        // row: a single ky*DH and kx*DW for kx = 0, 1, 2.
+        const float tyf = static_cast<float>(s.tap[tap0].x);
+        float txf[3];
 #pragma unroll
-        for (int i = 0; i < 3; ++i) {
-            const int2 tk = s.tap[tap0 + i];
-            tyf[i] = static_cast<float>(tk.x);
-            txf[i] = static_cast<float>(tk.y);
-        }
+        for (int i = 0; i < 3; ++i) txf[i] = static_cast<float>(s.tap[tap0 + i].y);
         uint32_t gi = 0, si = 0;
         bool ok = true;
         for (int u = blockIdx.x; u < a.num_units && ok; u += gridDim.x) {
@@ -454,7 +458,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                             off_x = raw_offset(off_x, __half2float(s.flow[st][0][r]));
                             mk = raw_mask(mk);
                         }
-                        const float y = (bfy[t] + tyf[i]) + off_y;
+                        const float y = (bfy[t] + tyf) + off_y;
                         const float x = (bfx[t] + txf[i]) + off_x;
                         m[i] = mk;
                         const int y0 = __float2int_rd(y);
@@ -473,30 +477,35 @@ __global__ void __launch_bounds__(kThreads, 1)
                     uint32_t outw[3][4];
 #pragma unroll
                     for (int i = 0; i < 3; ++i) {
-                        uint4 c00 = make_uint4(0u, 0u, 0u, 0u), c01 = c00, c10 = c00, c11 = c00;
                         if (in[i]) {
-                            c00 = lds128(base_addr[i]);
-                            c01 = lds128(base_addr[i] + 16);
-                            c10 = lds128(base_addr[i] + sw * 16);
-                            c11 = lds128(base_addr[i] + sw * 16 + 16);
-                        }
-                        const float mhy = m[i] * (1.0f - fy[i]);
-                        const float mly = m[i] * fy[i];
-                        const __half2 w00 = __float2half2_rn(mhy * (1.0f - fx[i]));
-                        const __half2 w01 = __float2half2_rn(mhy * fx[i]);
-                        const __half2 w10 = __float2half2_rn(mly * (1.0f - fx[i]));
-                        const __half2 w11 = __float2half2_rn(mly * fx[i]);
-                        const __half2 *h00 = reinterpret_cast<const __half2 *>(&c00);
-                        const __half2 *h01 = reinterpret_cast<const __half2 *>(&c01);
-                        const __half2 *h10 = reinterpret_cast<const __half2 *>(&c10);
-                        const __half2 *h11 = reinterpret_cast<const __half2 *>(&c11);
+                            const uint4 c00 = lds128(base_addr[i]);
+                            const uint4 c01 = lds128(base_addr[i] + 16);
+                            const uint4 c10 = lds128(base_addr[i] + sw * 16);
+                            const uint4 c11 = lds128(base_addr[i] + sw * 16 + 16);
+                            // The four bilinear weights, mask folded in, each rounded once to FP16
+                            // and packed in pairs: (top-left, top-right) and (bottom-left, bottom-right).
+                            const float mhy = m[i] * (1.0f - fy[i]);
+                            const float mly = m[i] * fy[i];
+                            const float hx = 1.0f - fx[i];
+                            const __half2 wt = __floats2half2_rn(mhy * hx, mhy * fx[i]);
+                            const __half2 wb = __floats2half2_rn(mly * hx, mly * fx[i]);
+                            const __half2 w00 = __low2half2(wt), w01 = __high2half2(wt);
+                            const __half2 w10 = __low2half2(wb), w11 = __high2half2(wb);
+                            const __half2 *h00 = reinterpret_cast<const __half2 *>(&c00);
+                            const __half2 *h01 = reinterpret_cast<const __half2 *>(&c01);
+                            const __half2 *h10 = reinterpret_cast<const __half2 *>(&c10);
+                            const __half2 *h11 = reinterpret_cast<const __half2 *>(&c11);
 #pragma unroll
-                        for (int e = 0; e < 4; ++e) {
-                            __half2 acc = __hmul2(w00, h00[e]);
-                            acc = __hfma2(w01, h01[e], acc);
-                            acc = __hfma2(w10, h10[e], acc);
-                            acc = __hfma2(w11, h11[e], acc);
-                            outw[i][e] = pack_half2(acc);
+                            for (int e = 0; e < 4; ++e) {
+                                __half2 acc = __hmul2(w00, h00[e]);
+                                acc = __hfma2(w01, h01[e], acc);
+                                acc = __hfma2(w10, h10[e], acc);
+                                acc = __hfma2(w11, h11[e], acc);
+                                outw[i][e] = pack_half2(acc);
+                            }
+                        } else {
+#pragma unroll
+                            for (int e = 0; e < 4; ++e) outw[i][e] = 0u;
                         }
                     }
                     if (!mbar_wait_bounded(&s.a_empty[st], ph ^ 1u, abort_flag)) {
@@ -504,11 +513,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                         break;
                     }
                     tc_fence_after();
-#pragma unroll
-                    for (int i = 0; i < 3; ++i)
-                        tmem_st_32x32b_x4(lane_base + kACol0 + st * kAStageCols + (tap0 + i) * 4, outw[i][0],
-                                          outw[i][1], outw[i][2], outw[i][3]);
-                    tmem_wait_st();
+                    tmem_st_32x32b_x12_wait(lane_base + kACol0 + st * kAStageCols + tap0 * 4, outw);
                     tc_fence_before();
                     __syncwarp();
                     if (lane == 0) mbar_arrive(&s.a_full[st]);

@@ -111,3 +111,106 @@ def compute_and_gather(compute, total_tiles: int, per_tile: int, dist, local=Non
         if ops:
             works.extend(dist.batch_isend_irecv(ops))
     return works
+
+
+class PeerGather:
+    """Writes every rank's output chunks straight into one tensor on the root GPU with the
+    copy engines (one cudaMemcpyAsync peer copy per chunk over NVLink), so no kernel and no SM
+    time is spent on the transfer and it overlaps the next chunk's kernels completely.
+
+    Root exports its full [total_tiles * per_tile] tensor through a CUDA IPC handle (plus the
+    tensor's offset inside its allocation), every other rank opens it in its own device's
+    address space.  `send` enqueues a chunk on the given stream; a copy is complete when that
+    stream reaches the end of it.  `close` unmaps the handle on every rank (all ranks call it,
+    followed by a barrier before root frees the tensor).  Host-side set-up uses the process group `dist` for the
+    handle exchange; the transfers themselves use no collective."""
+
+    def __init__(self, full, total_tiles: int, per_tile: int, dist, root: int = 0, element_size: int = 2):
+        import torch
+        from cuda.bindings import driver, runtime
+
+        self._rt = runtime
+        self.dist, self.root = dist, root
+        self.rank = dist.get_rank()
+        self.total_tiles, self.per_tile, self.es = total_tiles, per_tile, element_size
+        dev = torch.device("cuda", torch.cuda.current_device())
+        meta = torch.zeros(73, dtype=torch.uint8, device=dev)  # handle, offset, status byte
+        self._mapped = None
+        self.base = 0
+        problem = None
+        if self.rank == root:
+            ptr = full.data_ptr()
+            err, base, _size = driver.cuMemGetAddressRange(ptr)
+            if err == driver.CUresult.CUDA_SUCCESS:
+                err2, handle = runtime.cudaIpcGetMemHandle(int(base))
+                if err2 == runtime.cudaError_t.cudaSuccess:
+                    raw = bytes(handle.reserved) + int(ptr - int(base)).to_bytes(8, "little") + b"\x01"
+                    meta.copy_(torch.frombuffer(bytearray(raw), dtype=torch.uint8))
+                    self.base = ptr
+                else:
+                    problem = f"cudaIpcGetMemHandle failed: {err2}"
+            else:
+                problem = f"cuMemGetAddressRange failed: {err}"
+        # Every rank takes this broadcast, also when root could not export its tensor.
+        dist.broadcast(meta, src=root)
+        raw = bytes(meta.cpu().tolist())
+        if raw[72] != 1:
+            raise RuntimeError(problem or "root could not export its output tensor")
+        if self.rank != root:
+            handle = runtime.cudaIpcMemHandle_t()
+            handle.reserved = raw[:64]
+            offset = int.from_bytes(raw[64:72], "little")
+            err, mapped = runtime.cudaIpcOpenMemHandle(handle, runtime.cudaIpcMemLazyEnablePeerAccess)
+            if err != runtime.cudaError_t.cudaSuccess:
+                raise RuntimeError(f"cudaIpcOpenMemHandle failed: {err}")
+            self._mapped = int(mapped)
+            self.base = self._mapped + offset
+
+    def send(self, tile_begin: int, tile_end: int, src, stream) -> None:
+        """Copies `src` (this rank's output of tiles [tile_begin, tile_end)) into root's tensor."""
+        n = (tile_end - tile_begin) * self.per_tile * self.es
+        if n == 0 or self.rank == self.root:
+            return
+        if src.numel() * src.element_size() != n:
+            raise ValueError("chunk has the wrong size")
+        dst = self.base + tile_begin * self.per_tile * self.es
+        (err,) = self._rt.cudaMemcpyAsync(dst, src.data_ptr(), n, self._rt.cudaMemcpyKind.cudaMemcpyDefault,
+                                          stream.cuda_stream)
+        if err != self._rt.cudaError_t.cudaSuccess:
+            raise RuntimeError(f"peer copy failed: {err}")
+
+    def close(self) -> None:
+        """Unmaps root's tensor on this rank (after this rank's copies are done).  Not a
+        collective: the caller puts a barrier after every rank's close, before root frees."""
+        import torch
+
+        torch.cuda.synchronize()
+        if self._mapped is not None:
+            self._rt.cudaIpcCloseMemHandle(self._mapped)
+            self._mapped = None
+
+
+def compute_and_copy_to_root(compute, total_tiles: int, per_tile: int, dist, peer: PeerGather, local=None,
+                             full=None, root: int = 0, chunks: int = 4, copy_stream=None):
+    """compute_and_gather with the transfers made by the copy engines (PeerGather): after
+    `compute(b, e, dst)` has enqueued chunk [b, e) on the current stream, `copy_stream` waits for
+    it and copies the chunk into root's tensor while the current stream goes on with the next
+    chunk.  At the end the current stream waits for the copy stream, so an event recorded after
+    this call completes when this rank's outputs are all in root's memory."""
+    import torch
+
+    rank, world = dist.get_rank(), dist.get_world_size()
+    b, e = shard_range(total_tiles, rank, world)
+    cur = torch.cuda.current_stream()
+    copy_stream = copy_stream or torch.cuda.Stream()
+    for cb, ce in chunk_ranges(b, e, chunks):
+        if ce <= cb:
+            continue
+        if rank == root:
+            compute(cb, ce, full[cb * per_tile:ce * per_tile])
+            continue
+        dst = local[(cb - b) * per_tile:(ce - b) * per_tile]
+        compute(cb, ce, dst)
+        copy_stream.wait_stream(cur)
+        peer.send(cb, ce, dst, copy_stream)
+    cur.wait_stream(copy_stream)
