@@ -478,8 +478,11 @@ def run_ours(args):
         del raw, f1, f2, wsr
 
     # ---- final gather of every shard's output to rank 0 (N > 1) -------------------------
-    # (a) serial: the timed step's output sent after the step; (b) overlapped: the shard
-    # computed in chunks, each finished chunk sent to rank 0 while the next one is computed.
+    # (a) serial: the timed step's output sent to rank 0 after the step (NCCL point-to-point);
+    # (b) overlapped: every rank computes its shard in chunks and the copy engines copy each
+    #     finished chunk into rank 0's tensor (CUDA IPC peer copies) while the next is computed;
+    # (c) as (b) with rank 0 taking a larger share of the tiles when its NVLink ingress, not
+    #     compute, bounds (b): its own tiles never cross the link.
     gather = None
     if pg is not None and cfg["sharded"] and not cfg["f32"]:
         from jasnamacos_b200 import sharding
@@ -487,6 +490,8 @@ def run_ours(args):
         per_image = base_shape.output_count
         full = torch.empty(total_images * per_image, dtype=out.dtype, device=dev) if rank == 0 else None
         g_iters = 20
+        step()  # the plain step's output (the sections above wrote other results into `out`)
+        torch.cuda.synchronize(dev)
         serial = lambda: sharding.gather_to_root(out, total_images, per_image, pg, out=full)  # noqa: E731
         serial()  # connection set-up, untimed
         torch.cuda.synchronize(dev)
@@ -502,80 +507,83 @@ def run_ours(args):
         one = base_shape.with_batch(1)
         pin_, poff, pmsk = one.input_count, one.offset_count, one.mask_count
 
-        def compute(cb, ce, dst):
-            lb, le = cb - i_begin, ce - i_begin
-            op.forward_f16(one.with_batch(ce - cb), x[lb * pin_:le * pin_], off[lb * poff:le * poff],
-                           msk[lb * pmsk:le * pmsk], packed, b16, out=dst, flag=flag, workspace=ws)
+        def make_compute(first, xs, offs, msks):
+            def compute(cb, ce, dst):
+                lb, le = cb - first, ce - first
+                op.forward_f16(one.with_batch(ce - cb), xs[lb * pin_:le * pin_], offs[lb * poff:le * poff],
+                               msks[lb * pmsk:le * pmsk], packed, b16, out=dst, flag=flag, workspace=ws)
+            return compute
 
-        def overlapped():
-            for wk in sharding.compute_and_gather(compute, total_images, per_image, pg,
-                                                  local=out if rank != 0 else None, full=full,
-                                                  chunks=args.gather_chunks):
-                wk.wait()
-
-        for _ in range(3):
-            overlapped()
-        torch.cuda.synchronize(dev)
-        barrier(pg)
-        o_ms = max_over_ranks(event_time_ms(overlapped, g_iters) / g_iters, pg)
-        torch.cuda.synchronize(dev)
-        same = bool(torch.equal(full, serial_full)) if rank == 0 else True
-        same = max_over_ranks(0.0 if same else 1.0, pg) == 0.0
-        # (c) overlapped with copy-engine peer copies into rank 0's tensor (CUDA IPC)
-        peer_line = None
-        try:
-            peer = sharding.PeerGather(full, total_images, per_image, pg)
-        except Exception as exc:  # noqa: BLE001 - reported in the line; every rank takes the same path
-            peer, peer_line = None, {"unavailable": f"{type(exc).__name__}: {exc}"[:200]}
-        ok_all = max_over_ranks(0.0 if peer is not None else 1.0, pg) == 0.0
-        if ok_all:
+        def peer_pass(ranges, compute, local, label):
+            """Times one overlapped compute + copy-engine gather layout; every rank takes the same
+            collective steps, also when the IPC set-up fails on some rank."""
+            try:
+                peer = sharding.PeerGather(full, total_images, per_image, pg)
+            except Exception as exc:  # noqa: BLE001 - reported in the line
+                peer, problem = None, f"{type(exc).__name__}: {exc}"[:200]
+            ok_all = max_over_ranks(0.0 if peer is not None else 1.0, pg) == 0.0
+            if not ok_all:
+                if peer is not None:
+                    peer.close()
+                barrier(pg)
+                return {"unavailable": problem if peer is None else "IPC set-up failed on another rank"}
             if rank == 0:
                 full.zero_()
             torch.cuda.synchronize(dev)
             barrier(pg)
             copy_stream = torch.cuda.Stream(device=dev)
 
-            def overlapped_peer():
-                sharding.compute_and_copy_to_root(compute, total_images, per_image, pg, peer,
-                                                  local=out if rank != 0 else None, full=full,
-                                                  chunks=args.gather_chunks, copy_stream=copy_stream)
+            def run():
+                sharding.compute_and_copy_to_root(compute, total_images, per_image, pg, peer, local=local, full=full,
+                                                  chunks=args.gather_chunks, copy_stream=copy_stream, ranges=ranges)
 
             for _ in range(3):
-                overlapped_peer()
+                run()
             torch.cuda.synchronize(dev)
             barrier(pg)
-            p_ms = max_over_ranks(event_time_ms(overlapped_peer, g_iters) / g_iters, pg)
+            p_ms = max_over_ranks(event_time_ms(run, g_iters) / g_iters, pg)
             torch.cuda.synchronize(dev)
             barrier(pg)  # every peer copy has landed before rank 0 compares
-            psame = bool(torch.equal(full, serial_full)) if rank == 0 else True
-            psame = max_over_ranks(0.0 if psame else 1.0, pg) == 0.0
+            same = bool(torch.equal(full, serial_full)) if rank == 0 else True
+            same = max_over_ranks(0.0 if same else 1.0, pg) == 0.0
             peer.close()
             barrier(pg)
-            peer_line = {"ms_per_step": p_ms, "chunks": args.gather_chunks,
-                         "value_with_gather": job_px / (p_ms * 1e-3) / 1e6,
-                         "what": "as overlapped, but each finished chunk is copied into rank 0's tensor by the "
-                                 "copy engines (cudaMemcpyAsync peer copy over NVLink through a CUDA IPC "
-                                 "mapping) on a side stream: no kernel, no SM time for the transfer",
-                         "output_equals_serial_gather": psame}
-        else:
-            if peer is not None:
-                peer.close()
-            barrier(pg)
+            return {"ms_per_step": p_ms, "chunks": args.gather_chunks, "tiles_per_rank": [e - b for b, e in ranges],
+                    "value_with_gather": job_px / (p_ms * 1e-3) / 1e6, "output_equals_serial_gather": same,
+                    "what": label}
+
+        uniform = [sharding.shard_range(total_images, r, world) for r in range(world)]
+        peer_uniform = peer_pass(uniform, make_compute(i_begin, x, off, msk), out if rank != 0 else None,
+                                 "each rank computes its even shard in chunks; the copy engines copy every finished "
+                                 "chunk into rank 0's tensor (cudaMemcpyAsync peer copy over NVLink through a CUDA "
+                                 "IPC mapping) on a side stream while the next chunk is computed; the step ends when "
+                                 "rank 0 holds every output")
+        # Rank 0's share from the measured rates: compute time per tile on one GPU and ingress
+        # time per tile into rank 0, balanced so that both finish together.
+        t_c = ms_per_step / max(i_end - i_begin, 1)
+        t_i = root_ms / max(total_images - (uniform[0][1] - uniform[0][0]), 1)
+        share = t_i / (t_c + t_i)
+        peer_weighted = None
+        if share > 1.0 / world + 0.01:
+            ranges = sharding.weighted_ranges(total_images, world, 0, share)
+            wb, we = ranges[rank]
+            _, _, xw, offw, mskw, _, _ = synthetic.bench_inputs(args.config, rank, world, dev, total_images,
+                                                                images=(wb, we))
+            local_w = torch.empty((we - wb) * per_image, dtype=out.dtype, device=dev) if rank != 0 else None
+            peer_weighted = peer_pass(ranges, make_compute(wb, xw, offw, mskw), local_w,
+                                      f"as the even layout, but rank 0 takes {share:.3f} of the tiles (its compute "
+                                      "time then matches the other ranks' transfer into it)")
+            del xw, offw, mskw, local_w
         gather = {"serial": {"ms": g_ms, "root_ms": root_ms, "GB_s": recv_bytes / (g_ms * 1e-3) / 1e9,
                              "value_with_gather": job_px / ((ms_per_step + g_ms) * 1e-3) / 1e6,
                              "what": "the timed step's output shards to rank 0 after the step (NCCL point-to-point, "
                                      "receives posted together), max over ranks of 20 CUDA-event-timed iterations"},
-                  "overlapped": {"ms_per_step": o_ms, "chunks": args.gather_chunks,
-                                 "value_with_gather": job_px / (o_ms * 1e-3) / 1e6,
-                                 "what": "each rank computes its shard in chunks (dcn_forward_f16 per chunk) and sends "
-                                         "every finished chunk to rank 0 while the next is computed; rank 0 computes "
-                                         "into the gathered tensor; step ends when rank 0 holds every output",
-                                 "output_equals_serial_gather": same},
-                  "peer_copy": peer_line,
+                  "overlapped_peer_copy": peer_uniform, "overlapped_peer_copy_weighted": peer_weighted,
                   "bytes_to_root": recv_bytes, "unit": "Mpx/s"}
-        best = [gather["overlapped"]["value_with_gather"]]
-        if peer_line and "value_with_gather" in peer_line and peer_line["output_equals_serial_gather"]:
-            best.append(peer_line["value_with_gather"])
+        best = [gather["serial"]["value_with_gather"]]
+        for line in (peer_uniform, peer_weighted):
+            if line and line.get("output_equals_serial_gather"):
+                best.append(line["value_with_gather"])
         gather["value_with_gather"] = max(best)
         del full, serial_full
         torch.cuda.synchronize(dev)

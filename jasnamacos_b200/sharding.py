@@ -190,17 +190,36 @@ class PeerGather:
             self._mapped = None
 
 
+def weighted_ranges(total: int, world: int, root: int, root_share: float) -> list[tuple[int, int]]:
+    """Contiguous tile ranges for every rank, `root` taking round(root_share * total) tiles (at
+    least its even share) and the others splitting the rest evenly.  When the gather into root
+    is limited by root's NVLink ingress rather than by compute, root should compute more: its
+    own tiles never cross the link."""
+    own = max(total // world, min(total, int(round(root_share * total))))
+    rest = total - own
+    others = [r for r in range(world) if r != root]
+    sizes = {root: own}
+    for i, r in enumerate(others):
+        sizes[r] = rest * (i + 1) // len(others) - rest * i // len(others)
+    out, b = [], 0
+    for r in range(world):
+        out.append((b, b + sizes[r]))
+        b += sizes[r]
+    return out
+
+
 def compute_and_copy_to_root(compute, total_tiles: int, per_tile: int, dist, peer: PeerGather, local=None,
-                             full=None, root: int = 0, chunks: int = 4, copy_stream=None):
+                             full=None, root: int = 0, chunks: int = 4, copy_stream=None, ranges=None):
     """compute_and_gather with the transfers made by the copy engines (PeerGather): after
     `compute(b, e, dst)` has enqueued chunk [b, e) on the current stream, `copy_stream` waits for
     it and copies the chunk into root's tensor while the current stream goes on with the next
     chunk.  At the end the current stream waits for the copy stream, so an event recorded after
-    this call completes when this rank's outputs are all in root's memory."""
+    this call completes when this rank's outputs are all in root's memory.  `ranges` (one
+    (begin, end) per rank, e.g. weighted_ranges) replaces the even shard_range split."""
     import torch
 
     rank, world = dist.get_rank(), dist.get_world_size()
-    b, e = shard_range(total_tiles, rank, world)
+    b, e = ranges[rank] if ranges is not None else shard_range(total_tiles, rank, world)
     cur = torch.cuda.current_stream()
     copy_stream = copy_stream or torch.cuda.Stream()
     for cb, ce in chunk_ranges(b, e, chunks):

@@ -248,20 +248,36 @@ def bench_images(config: int, rank: int, world: int, total_tiles: int | None = N
     return 0, total
 
 
-def bench_inputs(config: int, rank: int, world: int, device, total_tiles: int | None = None):
-    """The device-resident inputs the benchmark times for `config` on `rank` of `world`:
-    (shape of the rank's batch, first image index, x, offset, mask, weight, bias).  A rank's
-    batch is seeded with BENCH_SEED + its first image index, so any rank's data -- and with it
-    any tile of a benchmarked shard -- can be rebuilt on any GPU for parity checks."""
+def device_tiles(config: int, begin: int, end: int, device):
+    """Benchmark images [begin, end) of `config` in device memory, image t generated from its
+    own seed BENCH_SEED + t with torch's generator (config 0 FP32, the others FP16), so every
+    image is the same whatever the rank layout: any benchmarked tile can be rebuilt on any GPU.
+    Returns (x, offset, mask, weight, bias); weight and bias (host FP32) are `weights`."""
     import torch
 
-    b, e = bench_images(config, rank, world, total_tiles)
+    one = config_shape(config, batch=1)
+    n = end - begin
+    dtype = torch.float32 if config == 0 else torch.float16
+    x = torch.empty(n * one.input_count, dtype=dtype, device=device)
+    off = torch.empty(n * one.offset_count, dtype=dtype, device=device)
+    msk = torch.empty(n * one.mask_count, dtype=dtype, device=device)
+    for k, t in enumerate(range(begin, end)):
+        if FLOW_RANGE[config] is None:
+            xi, oi, mi, _, _ = device_gaussian_batch(one, seed=BENCH_SEED + t, device=device, dtype=dtype)
+        else:
+            xi, oi, mi, _, _ = device_batch(one, FLOW_RANGE[config], seed=BENCH_SEED + t, device=device)
+        x[k * one.input_count:(k + 1) * one.input_count].copy_(xi)
+        off[k * one.offset_count:(k + 1) * one.offset_count].copy_(oi)
+        msk[k * one.mask_count:(k + 1) * one.mask_count].copy_(mi)
+    w, b = weights(one, CONFIG_SEED)
+    return x, off, msk, w, b
+
+
+def bench_inputs(config: int, rank: int, world: int, device, total_tiles: int | None = None,
+                 images: tuple[int, int] | None = None):
+    """The device-resident inputs the benchmark times for `config` on `rank` of `world` (or for
+    the explicit image range `images`): (shape of the rank's batch, first image index, x,
+    offset, mask, weight, bias), generated by device_tiles."""
+    b, e = images if images is not None else bench_images(config, rank, world, total_tiles)
     shape = config_shape(config, batch=1).with_batch(e - b)
-    seed = BENCH_SEED + b
-    if config == 0:
-        data = device_gaussian_batch(shape, seed=seed, device=device, dtype=torch.float32)
-    elif FLOW_RANGE[config] is None:
-        data = device_gaussian_batch(shape, seed=seed, device=device)
-    else:
-        data = device_batch(shape, FLOW_RANGE[config], seed=seed, device=device)
-    return (shape, b) + tuple(data)
+    return (shape, b) + tuple(device_tiles(config, b, e, device))
