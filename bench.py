@@ -480,9 +480,7 @@ def run_ours(args):
     # ---- final gather of every shard's output to rank 0 (N > 1) -------------------------
     # (a) serial: the timed step's output sent to rank 0 after the step (NCCL point-to-point);
     # (b) overlapped: every rank computes its shard in chunks and the copy engines copy each
-    #     finished chunk into rank 0's tensor (CUDA IPC peer copies) while the next is computed;
-    # (c) as (b) with rank 0 taking a larger share of the tiles when its NVLink ingress, not
-    #     compute, bounds (b): its own tiles never cross the link.
+    #     finished chunk into rank 0's tensor (CUDA IPC peer copies) while the next is computed.
     gather = None
     if pg is not None and cfg["sharded"] and not cfg["f32"]:
         from jasnamacos_b200 import sharding
@@ -558,32 +556,15 @@ def run_ours(args):
                                  "chunk into rank 0's tensor (cudaMemcpyAsync peer copy over NVLink through a CUDA "
                                  "IPC mapping) on a side stream while the next chunk is computed; the step ends when "
                                  "rank 0 holds every output")
-        # Rank 0's share from the measured rates: compute time per tile on one GPU and ingress
-        # time per tile into rank 0, balanced so that both finish together.
-        t_c = ms_per_step / max(i_end - i_begin, 1)
-        t_i = root_ms / max(total_images - (uniform[0][1] - uniform[0][0]), 1)
-        share = t_i / (t_c + t_i)
-        peer_weighted = None
-        if share > 1.0 / world + 0.01:
-            ranges = sharding.weighted_ranges(total_images, world, 0, share)
-            wb, we = ranges[rank]
-            _, _, xw, offw, mskw, _, _ = synthetic.bench_inputs(args.config, rank, world, dev, total_images,
-                                                                images=(wb, we))
-            local_w = torch.empty((we - wb) * per_image, dtype=out.dtype, device=dev) if rank != 0 else None
-            peer_weighted = peer_pass(ranges, make_compute(wb, xw, offw, mskw), local_w,
-                                      f"as the even layout, but rank 0 takes {share:.3f} of the tiles (its compute "
-                                      "time then matches the other ranks' transfer into it)")
-            del xw, offw, mskw, local_w
         gather = {"serial": {"ms": g_ms, "root_ms": root_ms, "GB_s": recv_bytes / (g_ms * 1e-3) / 1e9,
                              "value_with_gather": job_px / ((ms_per_step + g_ms) * 1e-3) / 1e6,
                              "what": "the timed step's output shards to rank 0 after the step (NCCL point-to-point, "
                                      "receives posted together), max over ranks of 20 CUDA-event-timed iterations"},
-                  "overlapped_peer_copy": peer_uniform, "overlapped_peer_copy_weighted": peer_weighted,
+                  "overlapped_peer_copy": peer_uniform,
                   "bytes_to_root": recv_bytes, "unit": "Mpx/s"}
         best = [gather["serial"]["value_with_gather"]]
-        for line in (peer_uniform, peer_weighted):
-            if line and line.get("output_equals_serial_gather"):
-                best.append(line["value_with_gather"])
+        if peer_uniform and peer_uniform.get("output_equals_serial_gather"):
+            best.append(peer_uniform["value_with_gather"])
         gather["value_with_gather"] = max(best)
         del full, serial_full
         torch.cuda.synchronize(dev)

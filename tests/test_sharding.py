@@ -119,3 +119,20 @@ def test_compute_and_gather_gloo(world, total, chunks):
     chunk is sent to rank 0 (some chunks empty when a shard is shorter than the chunk count)."""
     results = _run(world, total, per_tile=5, mode="pipelined", chunks=chunks)
     assert all(kind == "ok" and flag for kind, flag in results), results
+
+
+def test_weighted_ranges_and_sample_tiles():
+    from jasnamacos_b200.sharding import chunk_ranges, sample_tiles, weighted_ranges
+
+    for total, world, share in ((2048, 8, 0.19), (2048, 2, 0.1), (7, 3, 0.5), (100, 4, 1.0)):
+        ranges = weighted_ranges(total, world, 0, share)
+        assert ranges[0][0] == 0 and ranges[-1][1] == total
+        assert all(e0 == b1 for (_, e0), (b1, _) in zip(ranges, ranges[1:]))
+        assert ranges[0][1] - ranges[0][0] >= total // world  # root never below its even share
+        rest = [e - b for b, e in ranges[1:]]
+        assert max(rest) - min(rest) <= 1
+    assert weighted_ranges(2048, 8, 0, 0.19)[0] == (0, 389)
+    assert chunk_ranges(256, 512, 4) == [(256, 320), (320, 384), (384, 448), (448, 512)]
+    s = sample_tiles(2048, 8, 16)
+    assert len(s) == 128 and s[0] == 0 and s[-1] == 2047 and 255 in s and 256 in s
+    assert sample_tiles(128, 8, 2) == [0, 15, 16, 31, 32, 47, 48, 63, 64, 79, 80, 95, 96, 111, 112, 127]
