@@ -606,7 +606,8 @@ __global__ void __launch_bounds__(256) slab_reduce_kernel(Params p, const float 
 // 16-byte slab positions.  Needs W % 4 == 0 and 8-byte aligned channel planes.  Thread
 // j < W/4 of padded row py writes positions 4j+1 .. 4j+4; thread j == W/4 writes the
 // two border columns 0 and W+1; the border rows 0 and H+1 are all zeros.
-__global__ void __launch_bounds__(256) regroup_slabs_x4_kernel(const SplitInput<__half> in, uint4 *__restrict__ out,
+template <int kBlock, int kMinBlocks>
+__global__ void __launch_bounds__(kBlock, kMinBlocks) regroup_slabs_x4_kernel(const SplitInput<__half> in, uint4 *__restrict__ out,
                                                                 int N, int H, int W) {
     allow_dependent_launch();  // the slab kernel may start its set-up
     const int per_row = W / 4 + 1;
@@ -764,9 +765,19 @@ cudaError_t launch_regroup_slabs(const Params &p, const SplitInput<__half> &inpu
                      (input.second == nullptr || (reinterpret_cast<uintptr_t>(input.second) & 7u) == 0);
     if (vec) {
         const int threads = (p.H + 2) * (p.W / 4 + 1);
-        const dim3 grid(static_cast<unsigned>((threads + 255) / 256), static_cast<unsigned>(p.C / 8), images);
-        slab::regroup_slabs_x4_kernel<<<grid, 256, 0, stream>>>(input, static_cast<uint4 *>(workspace), p.N, p.H,
-                                                                 p.W);
+        if (slab_group_splits(p) > 1) {
+            // Small batches: 128-thread blocks of at most 32 registers, one of which fits on an
+            // SM next to a slab kernel block (640 threads x 96 registers), so the slab kernel's
+            // blocks, launched as programmatic dependents, become resident and do their set-up
+            // while the pre-pass still runs.
+            const dim3 grid(static_cast<unsigned>((threads + 127) / 128), static_cast<unsigned>(p.C / 8), images);
+            slab::regroup_slabs_x4_kernel<128, 16><<<grid, 128, 0, stream>>>(input, static_cast<uint4 *>(workspace),
+                                                                             p.N, p.H, p.W);
+        } else {
+            const dim3 grid(static_cast<unsigned>((threads + 255) / 256), static_cast<unsigned>(p.C / 8), images);
+            slab::regroup_slabs_x4_kernel<256, 1><<<grid, 256, 0, stream>>>(input, static_cast<uint4 *>(workspace),
+                                                                            p.N, p.H, p.W);
+        }
     } else {
         const int positions = (p.H + 2) * (p.W + 2);
         const dim3 grid(static_cast<unsigned>((positions + 255) / 256), static_cast<unsigned>(p.C / 8), images);
