@@ -512,7 +512,7 @@ def run_ours(args):
                                msks[lb * pmsk:le * pmsk], packed, b16, out=dst, flag=flag, workspace=ws)
             return compute
 
-        def peer_pass(ranges, compute, local, label):
+        def peer_pass(ranges, compute, local, label, chunks):
             """Times one overlapped compute + copy-engine gather layout; every rank takes the same
             collective steps, also when the IPC set-up fails on some rank."""
             try:
@@ -533,7 +533,7 @@ def run_ours(args):
 
             def run():
                 sharding.compute_and_copy_to_root(compute, total_images, per_image, pg, peer, local=local, full=full,
-                                                  chunks=args.gather_chunks, copy_stream=copy_stream, ranges=ranges)
+                                                  chunks=chunks, copy_stream=copy_stream, ranges=ranges)
 
             for _ in range(3):
                 run()
@@ -546,21 +546,27 @@ def run_ours(args):
             same = max_over_ranks(0.0 if same else 1.0, pg) == 0.0
             peer.close()
             barrier(pg)
-            return {"ms_per_step": p_ms, "chunks": args.gather_chunks, "tiles_per_rank": [e - b for b, e in ranges],
+            return {"ms_per_step": p_ms, "chunks": chunks, "tiles_per_rank": [e - b for b, e in ranges],
                     "value_with_gather": job_px / (p_ms * 1e-3) / 1e6, "output_equals_serial_gather": same,
                     "what": label}
 
         uniform = [sharding.shard_range(total_images, r, world) for r in range(world)]
-        peer_uniform = peer_pass(uniform, make_compute(i_begin, x, off, msk), out if rank != 0 else None,
-                                 "each rank computes its even shard in chunks; the copy engines copy every finished "
-                                 "chunk into rank 0's tensor (cudaMemcpyAsync peer copy over NVLink through a CUDA "
-                                 "IPC mapping) on a side stream while the next chunk is computed; the step ends when "
-                                 "rank 0 holds every output")
+        peer_lines = []
+        for chunks in [int(c) for c in str(args.gather_chunks).split(",") if c.strip()]:
+            peer_lines.append(peer_pass(
+                uniform, make_compute(i_begin, x, off, msk), out if rank != 0 else None,
+                "each rank computes its even shard in chunks; the copy engines copy every finished chunk into "
+                "rank 0's tensor (cudaMemcpyAsync peer copy over NVLink through a CUDA IPC mapping) on a side "
+                "stream while the next chunk is computed; the step ends when rank 0 holds every output", chunks))
+        valid = [ln for ln in peer_lines if ln.get("output_equals_serial_gather")]
+        peer_uniform = max(valid, key=lambda ln: ln["value_with_gather"]) if valid else (peer_lines[0] if peer_lines
+                                                                                          else None)
         gather = {"serial": {"ms": g_ms, "root_ms": root_ms, "GB_s": recv_bytes / (g_ms * 1e-3) / 1e9,
                              "value_with_gather": job_px / ((ms_per_step + g_ms) * 1e-3) / 1e6,
                              "what": "the timed step's output shards to rank 0 after the step (NCCL point-to-point, "
                                      "receives posted together), max over ranks of 20 CUDA-event-timed iterations"},
                   "overlapped_peer_copy": peer_uniform,
+                  "overlapped_peer_copy_by_chunks": [{k: v for k, v in ln.items() if k != "what"} for ln in peer_lines],
                   "bytes_to_root": recv_bytes, "unit": "Mpx/s"}
         best = [gather["serial"]["value_with_gather"]]
         if peer_uniform and peer_uniform.get("output_equals_serial_gather"):
@@ -698,8 +704,9 @@ def main():
     ap.add_argument("--no-raw", action="store_true", help="skip the fused offset-producer measurement")
     ap.add_argument("--graph", choices=("auto", "on", "off"), default="auto",
                     help="time steps as CUDA graph replays (auto: for the single-image configs 0, 1, 3)")
-    ap.add_argument("--gather-chunks", type=int, default=4,
-                    help="N > 1: chunks per shard in the overlapped compute + gather pass")
+    ap.add_argument("--gather-chunks", default="4,8",
+                    help="N > 1: chunks per shard in the overlapped compute + gather pass (comma list; the best "
+                         "verified one is reported)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--e2e-steps", type=int, default=5)
     ap.add_argument("--no-cpu-baseline", action="store_true")
