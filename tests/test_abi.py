@@ -168,3 +168,34 @@ def test_io_plumbing_is_validated_before_device_work(lib):
                 _native.DcnIo(None, 0, 192, -1)):
         assert call(ctypes.byref(bad)) == _native.DCN_ERR_INVALID_ARGUMENT
         assert raw_call(ctypes.byref(bad)) == _native.DCN_ERR_INVALID_ARGUMENT
+
+
+def test_host_entry_sizes_and_argument_checks(lib):
+    """dcn_forward_f16_host's staging workspace: up to three chunks in flight, each holding the
+    chunk's input, offset, mask, output and the operator's own workspace (the larger of a full
+    chunk's and the short last chunk's), plus one flag word; 0 for direct-path shapes.  Bad
+    arguments are rejected before the device is touched."""
+    one = DeformConvShape.jasna_propagation(1)
+    per = 2 * (one.input_count + one.offset_count + one.mask_count + one.output_count)
+    for batch, chunk in ((2048, 64), (5, 2), (3, 0), (1, 1)):
+        s = DeformConvShape.jasna_propagation(batch)
+        c = ctypes.byref(s.to_c())
+        eff = min(chunk or 64, batch)
+        slots = min(3, -(-batch // eff))
+        got = lib.dcn_forward_f16_host_workspace_bytes(c, chunk)
+        ws_chunk = lib.dcn_forward_f16_workspace_bytes(ctypes.byref(s.with_batch(eff).to_c()))
+        assert got >= 256 + slots * (eff * per + ws_chunk), (batch, chunk)
+        assert got < 256 + slots * (eff * per + 2 * ws_chunk + 4 * (1 << 20)), (batch, chunk)
+    small = DeformConvShape(1, 4, 5, 5, 3, 5, 5, 3, 3, 1, 1, 1, 1, 1, 1, 1, 1)  # direct path
+    assert lib.dcn_forward_f16_host_workspace_bytes(ctypes.byref(small.to_c()), 0) == 0
+    s = DeformConvShape.jasna_propagation(4).to_c()
+    p = ctypes.c_void_p(256)
+    need = lib.dcn_forward_f16_host_workspace_bytes(ctypes.byref(s), 2)
+    assert lib.dcn_forward_f16_host(ctypes.byref(s), p, p, p, p, p, p, None, 2, p, need - 1, None) == \
+        _native.DCN_ERR_INVALID_ARGUMENT
+    assert lib.dcn_forward_f16_host(ctypes.byref(s), p, p, p, p, p, p, None, -1, p, need, None) == \
+        _native.DCN_ERR_INVALID_ARGUMENT
+    assert lib.dcn_forward_f16_host(ctypes.byref(s), None, p, p, p, p, p, None, 2, p, need, None) == \
+        _native.DCN_ERR_INVALID_ARGUMENT
+    assert lib.dcn_forward_f16_host(ctypes.byref(small.to_c()), p, p, p, p, p, p, None, 0, p, need, None) == \
+        _native.DCN_ERR_UNSUPPORTED
