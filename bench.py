@@ -505,14 +505,16 @@ def run_ours(args):
         one = base_shape.with_batch(1)
         pin_, poff, pmsk = one.input_count, one.offset_count, one.mask_count
 
-        def make_compute(first, xs, offs, msks):
+        def make_compute(first, xs, offs, msks, wsp=None):
+            wsp = ws if wsp is None else wsp
+
             def compute(cb, ce, dst):
                 lb, le = cb - first, ce - first
                 op.forward_f16(one.with_batch(ce - cb), xs[lb * pin_:le * pin_], offs[lb * poff:le * poff],
-                               msks[lb * pmsk:le * pmsk], packed, b16, out=dst, flag=flag, workspace=ws)
+                               msks[lb * pmsk:le * pmsk], packed, b16, out=dst, flag=flag, workspace=wsp)
             return compute
 
-        def peer_pass(ranges, compute, local, label, chunks):
+        def peer_pass(ranges, compute, local, label, chunks, first_chunk=0, root_chunks=None):
             """Times one overlapped compute + copy-engine gather layout; every rank takes the same
             collective steps, also when the IPC set-up fails on some rank."""
             try:
@@ -533,7 +535,8 @@ def run_ours(args):
 
             def run():
                 sharding.compute_and_copy_to_root(compute, total_images, per_image, pg, peer, local=local, full=full,
-                                                  chunks=chunks, copy_stream=copy_stream, ranges=ranges)
+                                                  chunks=chunks, copy_stream=copy_stream, ranges=ranges,
+                                                  first_chunk=first_chunk, root_chunks=root_chunks)
 
             for _ in range(3):
                 run()
@@ -546,7 +549,8 @@ def run_ours(args):
             same = max_over_ranks(0.0 if same else 1.0, pg) == 0.0
             peer.close()
             barrier(pg)
-            return {"ms_per_step": p_ms, "chunks": chunks, "tiles_per_rank": [e - b for b, e in ranges],
+            return {"ms_per_step": p_ms, "chunks": chunks, "first_chunk": first_chunk, "root_chunks": root_chunks or chunks,
+                    "tiles_per_rank": [e - b for b, e in ranges],
                     "value_with_gather": job_px / (p_ms * 1e-3) / 1e6, "output_equals_serial_gather": same,
                     "what": label}
 
@@ -558,19 +562,49 @@ def run_ours(args):
                 "each rank computes its even shard in chunks; the copy engines copy every finished chunk into "
                 "rank 0's tensor (cudaMemcpyAsync peer copy over NVLink through a CUDA IPC mapping) on a side "
                 "stream while the next chunk is computed; the step ends when rank 0 holds every output", chunks))
+        # Root-weighted layout: rank 0's outputs never cross a link, so it takes the share at which
+        # its own compute (one launch) ends when the others' copies into it do -- from this run's
+        # compute time per image and the ingress time per image seen in the best even-layout pass
+        # (its time less its first chunk).  The others start with a short chunk so that the copies
+        # begin early.  Every rank computes the same share from max-over-ranks numbers.
+        timed = [ln for ln in peer_lines if ln.get("output_equals_serial_gather")]
+        if timed:
+            ref_line = min(timed, key=lambda ln: ln["ms_per_step"])
+            t_c = ms_per_step * 1e-3 / max(i_end - i_begin, 1)
+            even = total_images // world
+            t_i = max(ref_line["ms_per_step"] - ms_per_step / ref_line["chunks"], 1e-3) * 1e-3 / max(
+                total_images - even, 1)
+            first = max(1, even // 16)
+            while first < even and op.plan(base_shape.with_batch(first))["group_splits"] > 1:
+                first += 1  # a first chunk that takes the group split would change its images' bits
+            share = sharding.root_share_for_ingress(total_images, world, t_c, t_i, first)
+            if share > 1.0 / world + 0.01:
+                ranges = sharding.weighted_ranges(total_images, world, 0, share)
+                wb, we = ranges[rank]
+                _, _, xw, offw, mskw, _, _ = synthetic.bench_inputs(args.config, rank, world, dev, total_images,
+                                                                    images=(wb, we))
+                ws_w = torch.empty(op.workspace_bytes(base_shape.with_batch(we - wb)), dtype=torch.uint8, device=dev)
+                local_w = torch.empty((we - wb) * per_image, dtype=out.dtype, device=dev) if rank != 0 else None
+                peer_lines.append(peer_pass(
+                    ranges, make_compute(wb, xw, offw, mskw, ws_w), local_w,
+                    f"root-weighted layout: rank 0 computes {share:.3f} of the images in one launch straight into "
+                    f"the gathered tensor; the other ranks compute a first chunk of {first} images, then the rest "
+                    "in 4 chunks, each copied into rank 0's tensor by the copy engines while the next is computed",
+                    4, first_chunk=first, root_chunks=1))
+                del xw, offw, mskw, local_w, ws_w
         valid = [ln for ln in peer_lines if ln.get("output_equals_serial_gather")]
-        peer_uniform = max(valid, key=lambda ln: ln["value_with_gather"]) if valid else (peer_lines[0] if peer_lines
+        peer_best = max(valid, key=lambda ln: ln["value_with_gather"]) if valid else (peer_lines[0] if peer_lines
                                                                                           else None)
         gather = {"serial": {"ms": g_ms, "root_ms": root_ms, "GB_s": recv_bytes / (g_ms * 1e-3) / 1e9,
                              "value_with_gather": job_px / ((ms_per_step + g_ms) * 1e-3) / 1e6,
                              "what": "the timed step's output shards to rank 0 after the step (NCCL point-to-point, "
                                      "receives posted together), max over ranks of 20 CUDA-event-timed iterations"},
-                  "overlapped_peer_copy": peer_uniform,
+                  "overlapped_peer_copy": peer_best,
                   "overlapped_peer_copy_by_chunks": [{k: v for k, v in ln.items() if k != "what"} for ln in peer_lines],
                   "bytes_to_root": recv_bytes, "unit": "Mpx/s"}
         best = [gather["serial"]["value_with_gather"]]
-        if peer_uniform and peer_uniform.get("output_equals_serial_gather"):
-            best.append(peer_uniform["value_with_gather"])
+        if peer_best and peer_best.get("output_equals_serial_gather"):
+            best.append(peer_best["value_with_gather"])
         gather["value_with_gather"] = max(best)
         del full, serial_full
         torch.cuda.synchronize(dev)

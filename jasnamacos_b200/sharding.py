@@ -78,6 +78,26 @@ def chunk_ranges(begin: int, end: int, chunks: int) -> list[tuple[int, int]]:
     return [(begin + n * k // chunks, begin + n * (k + 1) // chunks) for k in range(chunks)]
 
 
+def pipeline_chunks(begin: int, end: int, chunks: int, first: int = 0) -> list[tuple[int, int]]:
+    """[begin, end) cut for a compute + copy pipeline: a short first chunk of `first` tiles (so
+    that the first copy starts early), then the rest in `chunks` near-equal chunks; without
+    `first` (or when the range is no longer than it), chunk_ranges(begin, end, chunks)."""
+    if 0 < first < end - begin:
+        return [(begin, begin + first)] + chunk_ranges(begin + first, end, chunks)
+    return chunk_ranges(begin, end, chunks)
+
+
+def root_share_for_ingress(total: int, world: int, compute_s_per_tile: float, ingress_s_per_tile: float,
+                           first: int = 0) -> float:
+    """Share of the tiles for the root of a copy-engine gather such that its own compute ends
+    when the others' outputs have arrived.  The root computes its R tiles in
+    R * compute_s_per_tile; the others start copying after their first chunk (`first` tiles) and
+    are then bound by the root's link ingress, (total - R) * ingress_s_per_tile.  Equal at
+    R = (total * ingress + first * compute) / (compute + ingress); never below the even share."""
+    r = (total * ingress_s_per_tile + first * compute_s_per_tile) / (compute_s_per_tile + ingress_s_per_tile)
+    return min(1.0, max(1.0 / world, r / total))
+
+
 def compute_and_gather(compute, total_tiles: int, per_tile: int, dist, local=None, full=None, root: int = 0,
                        chunks: int = 4):
     """One pass over this rank's tile shard with the gather to `root` overlapped: the shard is
@@ -209,20 +229,25 @@ def weighted_ranges(total: int, world: int, root: int, root_share: float) -> lis
 
 
 def compute_and_copy_to_root(compute, total_tiles: int, per_tile: int, dist, peer: PeerGather, local=None,
-                             full=None, root: int = 0, chunks: int = 4, copy_stream=None, ranges=None):
+                             full=None, root: int = 0, chunks: int = 4, copy_stream=None, ranges=None,
+                             first_chunk: int = 0, root_chunks: int | None = None):
     """compute_and_gather with the transfers made by the copy engines (PeerGather): after
     `compute(b, e, dst)` has enqueued chunk [b, e) on the current stream, `copy_stream` waits for
     it and copies the chunk into root's tensor while the current stream goes on with the next
     chunk.  At the end the current stream waits for the copy stream, so an event recorded after
     this call completes when this rank's outputs are all in root's memory.  `ranges` (one
-    (begin, end) per rank, e.g. weighted_ranges) replaces the even shard_range split."""
+    (begin, end) per rank, e.g. weighted_ranges) replaces the even shard_range split; the other
+    ranks cut their range with pipeline_chunks(..., chunks, first_chunk), root (whose outputs do
+    not move) into `root_chunks` chunks (default `chunks`)."""
     import torch
 
     rank, world = dist.get_rank(), dist.get_world_size()
     b, e = ranges[rank] if ranges is not None else shard_range(total_tiles, rank, world)
     cur = torch.cuda.current_stream()
     copy_stream = copy_stream or torch.cuda.Stream()
-    for cb, ce in chunk_ranges(b, e, chunks):
+    plan = (chunk_ranges(b, e, root_chunks or chunks) if rank == root
+            else pipeline_chunks(b, e, chunks, first_chunk))
+    for cb, ce in plan:
         if ce <= cb:
             continue
         if rank == root:

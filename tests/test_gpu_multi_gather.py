@@ -3,7 +3,8 @@
 Two ranks (one process per GPU, NCCL) each convolve their shard of a config-4-like batch chunk
 by chunk; every finished chunk reaches rank 0 either over NCCL point-to-point
 (sharding.compute_and_gather) or as a copy-engine peer copy into rank 0's tensor through a CUDA
-IPC mapping (sharding.PeerGather + compute_and_copy_to_root).  Rank 0 must end up with exactly
+IPC mapping (sharding.PeerGather + compute_and_copy_to_root), with even shards or with rank 0
+taking a larger share in one chunk and the others starting with a short chunk.  Rank 0 must end up with exactly
 the output a single dcn_forward_f16 call over the whole batch gives on its own GPU.  Skipped
 when fewer than two GPUs are visible.
 """
@@ -43,7 +44,7 @@ def _rank(rank, world, port, q):
         from jasnamacos_b200.deform_conv import CudaDeformConv
 
         op = CudaDeformConv(rank)
-        total, seed = 20, 5
+        total, seed = 40, 5
         full_shape = synthetic.config_shape(4, batch=total)
         x, off, msk, w, b = synthetic.device_batch(full_shape, 16.0, seed=seed, device="cuda")
         w16 = torch.from_numpy(w).cuda().half()
@@ -62,16 +63,31 @@ def _rank(rank, world, port, q):
                            off[cb * one.offset_count:ce * one.offset_count],
                            msk[cb * one.mask_count:ce * one.mask_count], packed, b16, out=dst)
 
+        # Root-weighted layout (rank 0 takes 70% of the images in one chunk, the other ranks start
+        # with a five-image chunk): the ranges differ from shard_range.  Every chunk keeps at least
+        # three 64x64 images (96 tiles), so no chunk takes the group split and every image's bits
+        # are those of the single call.
+        weighted = sharding.weighted_ranges(total, world, 0, 0.7)
+        wlo, whi = weighted[rank]
+        mine_w = op.forward_f16(full_shape.with_batch(whi - wlo), x[wlo * one.input_count:whi * one.input_count],
+                                off[wlo * one.offset_count:whi * one.offset_count],
+                                msk[wlo * one.mask_count:whi * one.mask_count], packed, b16) if rank else None
         results = {}
-        for mode in ("nccl", "peer"):
+        for mode in ("nccl", "peer", "peer_weighted"):
             full = torch.full((total * per,), float("nan"), dtype=torch.float16, device="cuda") if rank == 0 else None
-            local = torch.empty((hi - lo) * per, dtype=torch.float16, device="cuda") if rank else None
+            n_local = (whi - wlo) if mode == "peer_weighted" else (hi - lo)
+            local = torch.empty(n_local * per, dtype=torch.float16, device="cuda") if rank else None
             if mode == "nccl":
                 for wk in sharding.compute_and_gather(compute, total, per, dist, local=local, full=full, chunks=3):
                     wk.wait()
             else:
                 peer = sharding.PeerGather(full, total, per, dist)
-                sharding.compute_and_copy_to_root(compute, total, per, dist, peer, local=local, full=full, chunks=3)
+                if mode == "peer":
+                    sharding.compute_and_copy_to_root(compute, total, per, dist, peer, local=local, full=full,
+                                                      chunks=3)
+                else:
+                    sharding.compute_and_copy_to_root(compute, total, per, dist, peer, local=local, full=full,
+                                                      chunks=1, ranges=weighted, first_chunk=5, root_chunks=1)
                 torch.cuda.synchronize()
                 dist.barrier()
                 peer.close()
@@ -81,7 +97,7 @@ def _rank(rank, world, port, q):
             if rank == 0:
                 results[mode] = bool(torch.equal(full, ref))
             else:
-                results[mode] = bool(torch.equal(local, mine))
+                results[mode] = bool(torch.equal(local, mine_w if mode == "peer_weighted" else mine))
         q.put(("ok", rank, results))
     except Exception as exc:  # noqa: BLE001 - reported to the parent
         q.put(("error", rank, f"{type(exc).__name__}: {exc}"))
@@ -112,4 +128,4 @@ def test_overlapped_gather_two_gpus():
             p.kill()
     assert all(kind == "ok" for kind, _, _ in out), out
     for _, rank, res in out:
-        assert res == {"nccl": True, "peer": True}, (rank, res)
+        assert res == {"nccl": True, "peer": True, "peer_weighted": True}, (rank, res)

@@ -121,6 +121,26 @@ def test_compute_and_gather_gloo(world, total, chunks):
     assert all(kind == "ok" and flag for kind, flag in results), results
 
 
+def test_pipeline_chunks_and_root_share():
+    from jasnamacos_b200.sharding import chunk_ranges, pipeline_chunks, root_share_for_ingress
+
+    assert pipeline_chunks(0, 245, 4, 15) == [(0, 15)] + chunk_ranges(15, 245, 4)
+    assert pipeline_chunks(10, 20, 4) == chunk_ranges(10, 20, 4)
+    assert pipeline_chunks(10, 20, 2, 10) == chunk_ranges(10, 20, 2)  # first chunk not shorter than the range
+    for b, e, c, f in [(0, 245, 4, 15), (7, 8, 3, 1), (100, 356, 8, 16)]:
+        plan = pipeline_chunks(b, e, c, f)
+        assert plan[0][0] == b and plan[-1][1] == e
+        assert all(plan[i][1] == plan[i + 1][0] for i in range(len(plan) - 1))
+    # Root's compute ends when the ingress of the others' tiles (after their first chunk) does.
+    tc, ti = 3.45e-6, 0.655e-6
+    share = root_share_for_ingress(2048, 8, tc, ti, first=16)
+    r = share * 2048
+    assert abs(r * tc - (16 * tc + (2048 - r) * ti)) < 1e-9
+    assert root_share_for_ingress(2048, 8, 1.0, 1e-6) == 1.0 / 8  # fast links: never below the even share
+    assert root_share_for_ingress(16, 2, 1e-6, 1.0) > 0.999  # slow links: root keeps (almost) everything
+    assert root_share_for_ingress(16, 2, 1.0, 1.0, first=16) == 1.0  # capped at the whole batch
+
+
 def test_weighted_ranges_and_sample_tiles():
     from jasnamacos_b200.sharding import chunk_ranges, sample_tiles, weighted_ranges
 
