@@ -589,8 +589,8 @@ def run_ours(args):
                     ranges, make_compute(wb, xw, offw, mskw, ws_w), local_w,
                     f"root-weighted layout: rank 0 computes {share:.3f} of the images in one launch straight into "
                     f"the gathered tensor; the other ranks compute a first chunk of {first} images, then the rest "
-                    "in 4 chunks, each copied into rank 0's tensor by the copy engines while the next is computed",
-                    4, first_chunk=first, root_chunks=1))
+                    f"in {ref_line['chunks']} chunks, each copied into rank 0's tensor by the copy engines while "
+                    "the next is computed", ref_line["chunks"], first_chunk=first, root_chunks=1))
                 del xw, offw, mskw, local_w, ws_w
         valid = [ln for ln in peer_lines if ln.get("output_equals_serial_gather")]
         peer_best = max(valid, key=lambda ln: ln["value_with_gather"]) if valid else (peer_lines[0] if peer_lines
