@@ -444,7 +444,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                         ok = false;
                         break;
                     }
-                    float fy[3], fx[3], m[3];
+                    float fy[3], fx[3];
+                    __half m[3];
                     uint32_t base_addr[3];
                     bool in[3];
 #pragma unroll
@@ -452,11 +453,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                         const int k = tap0 + i;
                         float off_y = __half2float(s.off[st][2 * k][r]);
                         float off_x = __half2float(s.off[st][2 * k + 1][r]);
-                        float mk = __half2float(s.msk[st][k][r]);
+                        __half mk = s.msk[st][k][r];
                         if (FromRaw) {
                             off_y = raw_offset(off_y, __half2float(s.flow[st][1][r]));
                             off_x = raw_offset(off_x, __half2float(s.flow[st][0][r]));
-                            mk = raw_mask(mk);
+                            mk = __float2half_rn(raw_mask(__half2float(mk)));
                         }
                         const float y = (bfy[t] + tyf) + off_y;
                         const float x = (bfx[t] + txf[i]) + off_x;
@@ -482,13 +483,15 @@ __global__ void __launch_bounds__(kThreads, 1)
                             const uint4 c01 = lds128(base_addr[i] + 16);
                             const uint4 c10 = lds128(base_addr[i] + sw * 16);
                             const uint4 c11 = lds128(base_addr[i] + sw * 16 + 16);
-                            // The four bilinear weights, mask folded in, each rounded once to FP16
-                            // and packed in pairs: (top-left, top-right) and (bottom-left, bottom-right).
-                            const float mhy = m[i] * (1.0f - fy[i]);
-                            const float mly = m[i] * fy[i];
-                            const float hx = 1.0f - fx[i];
-                            const __half2 wt = __floats2half2_rn(mhy * hx, mhy * fx[i]);
-                            const __half2 wb = __floats2half2_rn(mly * hx, mly * fx[i]);
+                            // The four bilinear weights, mask folded in, in packed FP16 arithmetic:
+                            // (fy, fx) rounded to FP16, (1-fy, 1-fx), then (m(1-fy), m fy) and the
+                            // pairs (top-left, top-right), (bottom-left, bottom-right).
+                            const __half2 fyx = __floats2half2_rn(fy[i], fx[i]);
+                            const __half2 hyx = __hsub2(__float2half2_rn(1.0f), fyx);
+                            const __half2 my = __hmul2(__half2half2(m[i]), __lows2half2(hyx, fyx));
+                            const __half2 xx = __highs2half2(hyx, fyx);
+                            const __half2 wt = __hmul2(__low2half2(my), xx);
+                            const __half2 wb = __hmul2(__high2half2(my), xx);
                             const __half2 w00 = __low2half2(wt), w01 = __high2half2(wt);
                             const __half2 w10 = __low2half2(wb), w11 = __high2half2(wb);
                             const __half2 *h00 = reinterpret_cast<const __half2 *>(&c00);
