@@ -42,7 +42,7 @@ FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustain
 # What bounds each kernel below the HBM and tensor rooflines, from ncu captures of this build
 # (not measured by this script).
 LIMITERS = {
-    "slab_dcn_kernel": "shared-memory data pipe: 82.2% of peak LSU wavefronts (256-tile config-4 case); four random "
+    "slab_dcn_kernel": "shared-memory data pipe: 83.5% of peak LSU wavefronts (256-tile config-4 case); four random "
                        "16-byte loads per bilinear sample, about half of the wavefronts are bank-conflict replays",
     "fused_dcn_kernel": "L1 data pipe: ~72% of peak LSU wavefronts (config 3); scattered 32-byte corner-pair "
                         "loads from global memory, L1 hit rate ~8%",
