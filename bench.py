@@ -346,6 +346,70 @@ def event_time_ms(fn, iters: int, stream=None) -> float:
     return a.elapsed_time(b)
 
 
+# dcn_temporal_prepare_f16 algorithmic bytes per pixel: reads feat_prop, feat_current, feat_n2
+# (64 FP16 channels each), flow1 and the previous flow (2 each); writes the 196 condition
+# channels, flow2 (2) and, optionally, the 128-channel deform input.
+TEMPORAL_BYTES_PER_PX = 2 * (3 * 64 + 2 + 2) + 2 * (196 + 2)
+TEMPORAL_DEFORM_INPUT_BYTES_PER_PX = 2 * 128
+
+
+def temporal_section(op, dev, frames: int, steps: int, peaks: dict) -> dict:
+    """The temporal preparation in front of the DCN (dcn_temporal_prepare_f16) on `frames` 64x64
+    frames -- the benchmark's tile count -- with and without the deform-input copy: device time
+    (CUDA events), HBM roofline, and the first and last frames against the oracle (bit-exact)."""
+    import numpy as np
+    import torch
+
+    import oracle
+
+    w = h = 64
+    plane = w * h
+    g = torch.Generator(device=dev).manual_seed(4242)
+    feats = [torch.randn(frames * 64 * plane, generator=g, device=dev).half() for _ in range(3)]
+    flows = [(torch.rand(frames * 2 * plane, generator=g, device=dev) * 32 - 16).half() for _ in range(2)]
+    cond = torch.empty(frames * 196 * plane, dtype=torch.float16, device=dev)
+    di = torch.empty(frames * 128 * plane, dtype=torch.float16, device=dev)
+    flow2 = torch.empty(frames * 2 * plane, dtype=torch.float16, device=dev)
+
+    def run(with_di):
+        return lambda: op.temporal_prepare(w, h, *feats, *flows, True, batch=frames, conditions=cond,
+                                           deform_input=di if with_di else None, with_deform_input=with_di,
+                                           flow2=flow2)
+
+    out = {"frames": frames, "frame": "64x64, 64-channel features, flows U(-16,16) px",
+           "what": "flow2 = flow1 + warp(previous, flow1); conditions = [warp(feat_prop, flow1), feat_current, "
+                   "warp(feat_n2, flow2), flow1, flow2]; deform_input = [feat_prop, feat_n2] "
+                   "(runTemporalPreparation's two kernels as one)"}
+    for with_di in (True, False):
+        fn = run(with_di)
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize(dev)
+        ms = event_time_ms(fn, steps) / steps
+        bytes_px = TEMPORAL_BYTES_PER_PX + (TEMPORAL_DEFORM_INPUT_BYTES_PER_PX if with_di else 0)
+        gbs = bytes_px * frames * plane / (ms * 1e-3) / 1e9
+        key = "with_deform_input" if with_di else "without_deform_input"
+        out[key] = {"ms": ms, "Mpx_s": frames * plane / (ms * 1e-3) / 1e6, "GB_s": gbs,
+                    "frac_hbm": gbs / peaks["hbm_gbs"], "algorithmic_bytes_per_px": bytes_px}
+    run(True)()
+    torch.cuda.synchronize(dev)
+    mismatches, compared = 0, 0
+    for f in sorted({0, frames - 1}):
+        host = [t[f * c * plane:(f + 1) * c * plane].float().cpu().numpy() for t, c in
+                ((feats[0], 64), (feats[1], 64), (feats[2], 64), (flows[0], 2), (flows[1], 2))]
+        want = oracle.temporal_prepare(w, h, *host, True)
+        got = [t[f * c * plane:(f + 1) * c * plane].float().cpu().numpy() for t, c in
+               ((cond, 196), (di, 128), (flow2, 2))]
+        for a, b in zip(got, want):
+            mismatches += int(np.count_nonzero(a != b))
+            compared += a.size
+    out["parity"] = {"frames_compared": len({0, frames - 1}), "values_compared": compared,
+                     "mismatches": mismatches, "checker": "oracle.temporal_prepare (bit-exact expected)",
+                     "passed": mismatches == 0}
+    del feats, flows, cond, di, flow2
+    return out
+
+
 # Benchmark configurations.  Tile batches (2, 4) are sharded over the GPUs (total work
 # fixed: "strong"); single-image configurations (0, 1, 3) run one replica per GPU ("weak").
 CONFIGS = {
@@ -476,6 +540,12 @@ def run_ours(args):
                     "what": "dcn_forward_f16_raw: offset network output (3*G*9 ch) + two flows in, offsets/masks "
                             "computed inside the kernel (prepare_dcn_offsets_fp16 fused)"}
         del raw, f1, f2, wsr
+
+    # ---- temporal preparation in front of the DCN (config 4, one GPU) ---------------------
+    temporal = None
+    if args.config == 4 and world == 1 and not args.no_temporal:
+        temporal = temporal_section(op, dev, i_end - i_begin, args.steps, peaks)
+        torch.cuda.empty_cache()
 
     # ---- final gather of every shard's output to rank 0 (N > 1) -------------------------
     # (a) serial: the timed step's output sent to rank 0 after the step (NCCL point-to-point);
@@ -714,6 +784,7 @@ def run_ours(args):
             "parity": parity,
             "e2e": e2e,
             "raw_form": raw_form,
+            "temporal_prepare": temporal,
             "gather": gather,
             "gpu_launches": launches_per_step * args.steps,
             "clocks": clocks,
@@ -745,6 +816,8 @@ def main():
     ap.add_argument("--e2e-steps", type=int, default=5)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-parity", action="store_true", help="skip the oracle check of the timed output")
+    ap.add_argument("--no-temporal", action="store_true",
+                    help="skip the temporal-preparation measurement (config 4, one GPU)")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     args = ap.parse_args()
     if args.impl == "reference":

@@ -341,6 +341,25 @@ dcn_status dcn_flag_non_finite_f16(const void *values, int64_t count, uint32_t *
 dcn_status dcn_prepare_offsets_f16(int64_t plane, const void *raw, const void *flow1,
                                    const void *flow2, void *offset, void *mask, dcn_stream stream);
 
+/* ---- temporal preparation (the producers in front of the DCN) -----------------
+ * MetalDeformConv.runTemporalPreparation (MetalRunner.swift:510-582), i.e. the kernels
+ * accumulate_second_order_flow_fp16 + assemble_temporal_alignment_fp16
+ * (MetalShader.swift:736-813), for `batch` frames of width x height (the reference takes one
+ * frame).  Per frame, all FP16: feat_prop, feat_current, feat_n2 [64][H][W]; flow1 and
+ * previous_flow [2][H][W] in (x, y) order ->
+ *   flow2 [2][H][W]         = flow1 + warp(previous_flow, flow1) when has_second_order, else 0;
+ *   conditions [196][H][W]  = [warp(feat_prop, flow1), feat_current, warp(feat_n2, flow2),
+ *                              flow1, flow2] (the offset network's input);
+ *   deform_input [128][H][W] = [feat_prop, feat_n2] (the DCN's input; nullable: the DCN entry
+ *                              points read the two tensors directly through dcn_io).
+ * warp() is bilinear sampling with zero padding at (y + flow_y, x + flow_x) in FP32 on the FP16
+ * values, rounded to FP16 (flow2 is rounded before it warps feat_n2), as the reference computes
+ * it.  Frames are contiguous in every tensor. */
+dcn_status dcn_temporal_prepare_f16(int32_t batch, int32_t width, int32_t height, const void *feat_prop,
+                                    const void *feat_current, const void *feat_n2, const void *flow1,
+                                    const void *previous_flow, int32_t has_second_order, void *conditions,
+                                    void *deform_input, void *flow2, dcn_stream stream);
+
 /* ---- fused FP16 path without any caller allocation ----------------------------
  * No counterpart in the reference.  For callers that cannot allocate device
  * memory when they run the convolution (allocator-less or real-time regions,

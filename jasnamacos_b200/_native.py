@@ -137,6 +137,8 @@ PROTOTYPES = {
     ),
     "dcn_flag_non_finite_f16": (ctypes.c_int, [_P, ctypes.c_int64, _P, _P]),
     "dcn_prepare_offsets_f16": (ctypes.c_int, [ctypes.c_int64, _P, _P, _P, _P, _P, _P]),
+    "dcn_temporal_prepare_f16": (ctypes.c_int, [ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, _P, _P, _P, _P, _P,
+                                                ctypes.c_int32, _P, _P, _P, _P]),
     "dcn_device_error": (ctypes.c_int, []),
     "dcn_check_wait_timeout": (ctypes.c_int, [ctypes.c_uint32, _P]),
     "dcn_forward_f16_host_workspace_bytes": (ctypes.c_size_t, [_SHAPE, ctypes.c_int32]),

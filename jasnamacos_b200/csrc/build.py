@@ -32,6 +32,7 @@ SOURCES = [
     "dcn_aux.cu",
     "dcn_static_scratch.cu",
     "dcn_host.cu",
+    "dcn_temporal.cu",
 ]
 HEADERS = ["dcn_common.cuh"]
 

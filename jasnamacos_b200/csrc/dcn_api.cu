@@ -64,6 +64,11 @@ cudaError_t launch_slab_grouped(const Params &p, const void *slabs, const __half
                                 const uint8_t *packed_w, const __half *bias, __half *output, uint32_t *flag,
                                 int sm_count, uint32_t *err, cudaStream_t stream);
 
+cudaError_t launch_temporal_prepare(int n, int height, int width, const __half *feat_prop, const __half *feat_current,
+                                    const __half *feat_n2, const __half *flow1, const __half *previous,
+                                    bool has_second_order, __half *conditions, __half *deform_input, __half *flow2,
+                                    cudaStream_t stream);
+
 uint64_t current_context_id() {
     static PFN_cuCtxGetCurrent_v4000 get_current = nullptr;
     static PFN_cuCtxGetId_v12000 get_id = nullptr;
@@ -509,6 +514,29 @@ dcn_status dcn_flag_non_finite_f16(const void *values, int64_t count, uint32_t *
     if (st != DCN_OK) return st;
     return from_cuda(launch_flag_non_finite(static_cast<const __half *>(values), count, flag, dev->sm_count,
                                             reinterpret_cast<cudaStream_t>(stream)));
+}
+
+dcn_status dcn_temporal_prepare_f16(int32_t batch, int32_t width, int32_t height, const void *feat_prop,
+                                    const void *feat_current, const void *feat_n2, const void *flow1,
+                                    const void *previous_flow, int32_t has_second_order, void *conditions,
+                                    void *deform_input, void *flow2, dcn_stream stream) {
+    // runTemporalPreparation's guard (MetalRunner.swift:520-527): positive extents; the counts
+    // it checks are the caller's tensor sizes here.
+    if (batch <= 0 || width <= 0 || height <= 0 ||
+        static_cast<int64_t>(width) * height > (int64_t{1} << 31) / 256)
+        return DCN_ERR_INVALID_SHAPE;
+    const void *in[] = {feat_prop, feat_current, feat_n2, flow1, previous_flow, conditions, flow2};
+    for (const void *q : in)
+        if (q == nullptr || !aligned(q, 2)) return DCN_ERR_INVALID_ARGUMENT;
+    if (deform_input != nullptr && !aligned(deform_input, 2)) return DCN_ERR_INVALID_ARGUMENT;
+    DeviceInfo *dev = nullptr;
+    dcn_status st = current_device(&dev);
+    if (st != DCN_OK) return st;
+    return from_cuda(launch_temporal_prepare(
+        batch, height, width, static_cast<const __half *>(feat_prop), static_cast<const __half *>(feat_current),
+        static_cast<const __half *>(feat_n2), static_cast<const __half *>(flow1),
+        static_cast<const __half *>(previous_flow), has_second_order != 0, static_cast<__half *>(conditions),
+        static_cast<__half *>(deform_input), static_cast<__half *>(flow2), reinterpret_cast<cudaStream_t>(stream)));
 }
 
 dcn_status dcn_prepare_offsets_f16(int64_t plane, const void *raw, const void *flow1, const void *flow2,

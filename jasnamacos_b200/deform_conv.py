@@ -121,6 +121,15 @@ def raise_for_status(status: int, context: str = "") -> None:
 
 
 @dataclass(frozen=True)
+class TemporalPreparationResult:
+    """TemporalPreparationResult (MetalRunner.swift:60-65): FP16 host arrays."""
+    gpu_milliseconds: float
+    conditions: np.ndarray        # [196 * plane]
+    deform_input: np.ndarray      # [128 * plane]
+    second_order_flow: np.ndarray  # [2 * plane]
+
+
+@dataclass(frozen=True)
 class DeformConvShape:
     """`struct DeformConvShape` (DeformConv.swift:3-42), same fields in the same order."""
 
@@ -474,6 +483,36 @@ class CudaDeformConv:
         raise_for_status(st, "dcn_prepare_offsets_f16")
         return offset, mask
 
+    def temporal_prepare(self, width: int, height: int, feat_prop, feat_current, feat_n2, flow1, previous_flow,
+                         has_second_order: bool, batch: int = 1, conditions=None, deform_input=None,
+                         with_deform_input: bool = True, flow2=None, stream=None):
+        """accumulate_second_order_flow_fp16 + assemble_temporal_alignment_fp16
+        (MetalShader.swift:736-813) on device FP16 tensors for `batch` frames, through
+        dcn_temporal_prepare_f16.  Returns (conditions [batch*196*plane], deform_input
+        [batch*128*plane] or None when `with_deform_input` is false, flow2 [batch*2*plane])."""
+        torch = _torch()
+        plane = width * height
+        if width <= 0 or height <= 0 or batch <= 0:
+            raise InvalidShape()
+        for t, ch in ((feat_prop, 64), (feat_current, 64), (feat_n2, 64), (flow1, 2), (previous_flow, 2)):
+            if t.numel() != batch * ch * plane:
+                raise InvalidShape()
+        dev = feat_prop.device
+        if conditions is None:
+            conditions = torch.empty(batch * 196 * plane, dtype=torch.float16, device=dev)
+        if deform_input is None and with_deform_input:
+            deform_input = torch.empty(batch * 128 * plane, dtype=torch.float16, device=dev)
+        if flow2 is None:
+            flow2 = torch.empty(batch * 2 * plane, dtype=torch.float16, device=dev)
+        tensors = [feat_prop, feat_current, feat_n2, flow1, previous_flow, conditions, flow2]
+        self._check_device(*tensors, *([deform_input] if deform_input is not None else []))
+        st = self.lib.dcn_temporal_prepare_f16(batch, width, height, *[_ptr(t) for t in tensors[:5]],
+                                               1 if has_second_order else 0, _ptr(conditions),
+                                               _ptr(deform_input) if deform_input is not None else None,
+                                               _ptr(flow2), _stream_handle(stream))
+        raise_for_status(st, "dcn_temporal_prepare_f16")
+        return conditions, deform_input, flow2
+
     def device_error(self) -> None:
         """Raises DeviceTimeout if a kernel's bounded device-side wait expired since the last check."""
         raise_for_status(self.lib.dcn_device_error(), "device error word")
@@ -554,6 +593,29 @@ class CudaDeformConv:
         if int(flag.item()) & _native.DCN_FLAG_NONFINITE:
             raise NonFiniteOutput("Inf/NaN in the DCNv2 output")
         return out.cpu().numpy()
+
+    def run_temporal_preparation(self, width: int, height: int, feat_prop, feat_current, feat_n2, flow1,
+                                 previous_flow, has_second_order: bool) -> "TemporalPreparationResult":
+        """`runTemporalPreparation(width:height:featProp:featCurrent:featN2:flow1:previousFlow:
+        hasSecondOrder:)` (MetalRunner.swift:510-582): one frame of FP16 host arrays in, the
+        conditions, the deform input and the second-order flow out (FP16 host arrays), with the
+        GPU time of the call."""
+        torch = _torch()
+        plane = width * height
+        arrays = [np.ascontiguousarray(a, dtype=np.float16).reshape(-1)
+                  for a in (feat_prop, feat_current, feat_n2, flow1, previous_flow)]
+        if width <= 0 or height <= 0 or [a.size for a in arrays] != [64 * plane] * 3 + [2 * plane] * 2:
+            raise InvalidShape()
+        dev = self.device
+        ins = [torch.from_numpy(a).to(dev) for a in arrays]
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record()
+        cond, di, flow2 = self.temporal_prepare(width, height, *ins, has_second_order)
+        end.record()
+        end.synchronize()
+        self.device_error()
+        return TemporalPreparationResult(float(start.elapsed_time(end)), cond.cpu().numpy(), di.cpu().numpy(),
+                                         flow2.cpu().numpy())
 
     # -- benchmark (benchmarkJasnaShape) ----------------------------------------
     def benchmark_jasna_shape(self, iterations: int = 20, weight_set=None, seed: int = 0x4A41534E41):

@@ -65,6 +65,9 @@ def load():
             lib.dcn_oracle_run_sample.restype = ctypes.c_int
             lib.dcn_oracle_prepare_offsets.argtypes = [ctypes.c_int64, fp, fp, fp, fp, fp]
             lib.dcn_oracle_prepare_offsets.restype = None
+            lib.dcn_oracle_temporal_prepare.argtypes = [ctypes.c_int32, ctypes.c_int32, fp, fp, fp, fp, fp,
+                                                        ctypes.c_int, fp, fp, fp]
+            lib.dcn_oracle_temporal_prepare.restype = None
             lib.dcn_oracle_splitmix64.argtypes = [ctypes.POINTER(ctypes.c_uint64)]
             lib.dcn_oracle_splitmix64.restype = ctypes.c_uint64
             _lib = lib
@@ -125,6 +128,23 @@ def prepare_offsets(plane: int, raw, flow1, flow2):
     mask = np.zeros(144 * plane, dtype=np.float32)
     lib.dcn_oracle_prepare_offsets(plane, _fptr(raw), _fptr(flow1), _fptr(flow2), _fptr(offset), _fptr(mask))
     return offset, mask
+
+
+def temporal_prepare(width: int, height: int, feat_prop, feat_current, feat_n2, flow1, previous_flow,
+                     has_second_order: bool, deform_input: bool = True):
+    """runTemporalPreparation (MetalRunner.swift:510-582) for one frame on FP16-valued float
+    arrays: returns (conditions [196*plane], deform_input [128*plane] or None, flow2 [2*plane]),
+    float32 arrays holding FP16 values."""
+    lib = load()
+    plane = width * height
+    arrays = [np.ascontiguousarray(a, dtype=np.float32).reshape(-1)
+              for a in (feat_prop, feat_current, feat_n2, flow1, previous_flow)]
+    cond = np.zeros(196 * plane, dtype=np.float32)
+    di = np.zeros(128 * plane, dtype=np.float32) if deform_input else None
+    flow2 = np.zeros(2 * plane, dtype=np.float32)
+    lib.dcn_oracle_temporal_prepare(width, height, *[_fptr(a) for a in arrays], 1 if has_second_order else 0,
+                                    _fptr(cond), _fptr(di) if di is not None else None, _fptr(flow2))
+    return cond, di, flow2
 
 
 def splitmix64_sequence(seed: int, count: int) -> list[int]:

@@ -379,6 +379,56 @@ void dcn_oracle_prepare_offsets(int64_t plane, const float *raw, const float *fl
     }
 }
 
+/* FP16 rounding (round to nearest even) of a float: the reference stores every Metal
+ * result as `half`. */
+static float round_f16(float v) { return (float)(_Float16)v; }
+
+/* runTemporalPreparation (MetalRunner.swift:510-582): accumulate_second_order_flow_fp16
+ * (MetalShader.swift:739-762) and assemble_temporal_alignment_fp16 (:768-813), in the order of
+ * the reference's self-check (JasnaCLI.swift:248-290); `bilinear` is its `sampleZero`
+ * (:213-225), the same arithmetic as DeformConvCPU.bilinear. */
+void dcn_oracle_temporal_prepare(int32_t width, int32_t height, const float *feat_prop,
+                                 const float *feat_current, const float *feat_n2,
+                                 const float *flow1, const float *previous_flow,
+                                 int has_second_order, float *conditions, float *deform_input,
+                                 float *flow2) {
+    const int64_t w = width, h = height, plane = w * h;
+    for (int64_t c = 0; c < 2; ++c) {
+        for (int64_t p = 0; p < plane; ++p) {
+            if (!has_second_order) {
+                flow2[c * plane + p] = 0.0f;
+                continue;
+            }
+            const float y = (float)(p / w), x = (float)(p % w);
+            const float warped = bilinear(previous_flow, c * plane, h, w, y + flow1[plane + p], x + flow1[p]);
+            flow2[c * plane + p] = round_f16(flow1[c * plane + p] + warped);
+        }
+    }
+    for (int64_t c = 0; c < 196; ++c) {
+        for (int64_t p = 0; p < plane; ++p) {
+            const float y = (float)(p / w), x = (float)(p % w);
+            float v;
+            if (c < 64)
+                v = round_f16(bilinear(feat_prop, c * plane, h, w, y + flow1[plane + p], x + flow1[p]));
+            else if (c < 128)
+                v = feat_current[(c - 64) * plane + p];
+            else if (c < 192)
+                v = round_f16(bilinear(feat_n2, (c - 128) * plane, h, w, y + flow2[plane + p], x + flow2[p]));
+            else if (c < 194)
+                v = flow1[(c - 192) * plane + p];
+            else
+                v = flow2[(c - 194) * plane + p];
+            conditions[c * plane + p] = v;
+        }
+    }
+    if (deform_input != NULL) {
+        for (int64_t i = 0; i < 64 * plane; ++i) {
+            deform_input[i] = feat_prop[i];
+            deform_input[64 * plane + i] = feat_n2[i];
+        }
+    }
+}
+
 /* SeededGenerator.next (DeformConv.swift:175-181). */
 uint64_t dcn_oracle_splitmix64(uint64_t *state) {
     *state += 0x9E3779B97F4A7C15ULL;

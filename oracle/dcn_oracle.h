@@ -71,6 +71,22 @@ int dcn_oracle_run_sample(const dcn_oracle_shape *s, const float *input, const f
 void dcn_oracle_prepare_offsets(int64_t plane, const float *raw, const float *flow1,
                                 const float *flow2, float *offset, float *mask);
 
+/* MetalDeformConv.runTemporalPreparation (MetalRunner.swift:510-582) for one width x height
+ * frame: accumulate_second_order_flow_fp16 then assemble_temporal_alignment_fp16
+ * (MetalShader.swift:736-813), restated the way the reference's own self-check computes its
+ * expectations (JasnaCLI.swift:211-290, `sampleZero`): FP32 bilinear sampling with zero padding
+ * of FP16 values, every stored result rounded to FP16 (round to nearest even), flow2 rounded
+ * before it is used to warp feat_n2.  Inputs hold FP16 values widened to float:
+ * feat_* [64][plane], flow1 / previous_flow [2][plane] in (x, y) order.  Outputs (floats
+ * holding FP16 values): conditions [196][plane] = [warp(feat_prop, flow1), feat_current,
+ * warp(feat_n2, flow2), flow1, flow2], deform_input [128][plane] = [feat_prop, feat_n2]
+ * (may be NULL), flow2 [2][plane] (all zeros when has_second_order is 0). */
+void dcn_oracle_temporal_prepare(int32_t width, int32_t height, const float *feat_prop,
+                                 const float *feat_current, const float *feat_n2,
+                                 const float *flow1, const float *previous_flow,
+                                 int has_second_order, float *conditions, float *deform_input,
+                                 float *flow2);
+
 /* SplitMix64 step of SeededGenerator.next (DeformConv.swift:168-181). */
 uint64_t dcn_oracle_splitmix64(uint64_t *state);
 

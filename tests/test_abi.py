@@ -199,3 +199,22 @@ def test_host_entry_sizes_and_argument_checks(lib):
         _native.DCN_ERR_INVALID_ARGUMENT
     assert lib.dcn_forward_f16_host(ctypes.byref(small.to_c()), p, p, p, p, p, p, None, 0, p, need, None) == \
         _native.DCN_ERR_UNSUPPORTED
+
+
+def test_temporal_prepare_argument_checks(lib):
+    """dcn_temporal_prepare_f16 rejects bad extents and missing or misaligned tensors before it
+    touches a device (deform_input alone may be null)."""
+    p = ctypes.c_void_p(256)
+    odd = ctypes.c_void_p(257)
+    args = lambda **k: [k.get(n, p) for n in ("prop", "cur", "n2", "f1", "prev")]  # noqa: E731
+    call = lambda b, w, h, ins, cond=p, di=None, f2=p: lib.dcn_temporal_prepare_f16(  # noqa: E731
+        b, w, h, *ins, 1, cond, di, f2, None)
+    assert call(0, 64, 64, args()) == _native.DCN_ERR_INVALID_SHAPE
+    assert call(1, 0, 64, args()) == _native.DCN_ERR_INVALID_SHAPE
+    assert call(1, 64, -1, args()) == _native.DCN_ERR_INVALID_SHAPE
+    assert call(1, 1 << 16, 1 << 16, args()) == _native.DCN_ERR_INVALID_SHAPE
+    assert call(1, 64, 64, args(n2=None)) == _native.DCN_ERR_INVALID_ARGUMENT
+    assert call(1, 64, 64, args(f1=odd)) == _native.DCN_ERR_INVALID_ARGUMENT
+    assert call(1, 64, 64, args(), cond=None) == _native.DCN_ERR_INVALID_ARGUMENT
+    assert call(1, 64, 64, args(), f2=None) == _native.DCN_ERR_INVALID_ARGUMENT
+    assert call(1, 64, 64, args(), di=odd) == _native.DCN_ERR_INVALID_ARGUMENT

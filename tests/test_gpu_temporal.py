@@ -1,0 +1,105 @@
+"""GPU: dcn_temporal_prepare_f16, the temporal preparation in front of the DCN
+(runTemporalPreparation, MetalRunner.swift:510-582; kernels MetalShader.swift:736-813), against the
+oracle's restatement (oracle.temporal_prepare, pinned in tests/test_oracle_temporal.py).
+
+The kernel uses the reference's sampling arithmetic with one IEEE rounding per operation, so every
+output must equal the oracle's bit for bit: on the reference CLI's own 3x3 case
+(JasnaCLI.swift:227-316, also under its 0.004 gate), on the 64x64 frames of the reference's
+temporal probe (TemporalPreparationProbe.swift:14-101: its feature formula, its repeat and
+first-order-zero checks), batched, with and without the deform-input copy, and on a 270x480
+frame whose flows leave the frame on every side.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+import oracle
+from tests.test_oracle_temporal import cli_inputs
+
+pytestmark = pytest.mark.gpu
+
+
+def _probe_features(plane: int, seed: int) -> np.ndarray:
+    """features(seed:) of TemporalPreparationProbe.swift:23-27, FP16-rounded."""
+    i = np.arange(64 * plane, dtype=np.int64)
+    v = (((i * 37 + seed) % 509).astype(np.float32) / np.float32(508) - np.float32(0.5)) * np.float32(0.5)
+    return v.astype(np.float16).astype(np.float32)
+
+
+def _flows(plane: int, lim: float, seed: int) -> np.ndarray:
+    g = np.random.default_rng(seed)
+    return g.uniform(-lim, lim, 2 * plane).astype(np.float16).astype(np.float32)
+
+
+def test_cli_case_bit_exact(cuda_op):
+    ins = cli_inputs()
+    res = cuda_op.run_temporal_preparation(3, 3, *ins, True)
+    cond, di, flow2 = oracle.temporal_prepare(3, 3, *ins, True)
+    assert np.array_equal(res.second_order_flow.astype(np.float32), flow2)
+    assert np.array_equal(res.conditions.astype(np.float32), cond)
+    assert np.array_equal(res.deform_input.astype(np.float32), di)
+    got = np.concatenate([res.second_order_flow, res.conditions, res.deform_input]).astype(np.float32)
+    assert np.abs(got - np.concatenate([flow2, cond, di])).max() < 0.004  # JasnaCLI.swift:296
+    assert res.gpu_milliseconds >= 0.0
+    # first-order run (JasnaCLI.swift:300-313): the second-order flow is exactly zero
+    fp, fc, _, f1, prev = ins
+    first = cuda_op.run_temporal_preparation(3, 3, fp, fc, np.zeros(64 * 9, np.float32), f1, prev, False)
+    assert not np.any(first.second_order_flow)
+
+
+@pytest.mark.parametrize("second_order", [True, False], ids=["second_order", "first_order"])
+def test_probe_frames_batched_bit_exact(cuda_op, second_order):
+    """Three 64x64 frames in one call (the probe's features, flows up to +-16 px), compared frame by
+    frame with the oracle; the same call without the deform-input copy gives the same conditions
+    and flow; repeated calls are identical (the probe's repeat check)."""
+    import torch
+
+    w = h = 64
+    plane = w * h
+    frames = 3
+    ins = {k: [] for k in ("prop", "cur", "n2", "f1", "prev")}
+    for f in range(frames):
+        ins["prop"].append(_probe_features(plane, 17 + f))
+        ins["cur"].append(_probe_features(plane, 31 + f))
+        ins["n2"].append(_probe_features(plane, 47 + f) if second_order else np.zeros(64 * plane, np.float32))
+        ins["f1"].append(_flows(plane, 16.0, 100 + f))
+        ins["prev"].append(_flows(plane, 16.0, 200 + f))
+    dev = {k: torch.from_numpy(np.concatenate(v).astype(np.float16)).cuda() for k, v in ins.items()}
+    args = (w, h, dev["prop"], dev["cur"], dev["n2"], dev["f1"], dev["prev"], second_order)
+    cond, di, flow2 = cuda_op.temporal_prepare(*args, batch=frames)
+    cond2, none, flow2b = cuda_op.temporal_prepare(*args, batch=frames, with_deform_input=False)
+    again, _, _ = cuda_op.temporal_prepare(*args, batch=frames)
+    torch.cuda.synchronize()
+    cuda_op.device_error()
+    assert none is None
+    assert torch.equal(cond, cond2) and torch.equal(flow2, flow2b) and torch.equal(cond, again)
+    cond_h, di_h, flow2_h = (t.float().cpu().numpy() for t in (cond, di, flow2))
+    for f in range(frames):
+        want = oracle.temporal_prepare(w, h, ins["prop"][f], ins["cur"][f], ins["n2"][f], ins["f1"][f],
+                                       ins["prev"][f], second_order)
+        assert np.array_equal(cond_h[f * 196 * plane:(f + 1) * 196 * plane], want[0]), f
+        assert np.array_equal(di_h[f * 128 * plane:(f + 1) * 128 * plane], want[1]), f
+        assert np.array_equal(flow2_h[f * 2 * plane:(f + 1) * 2 * plane], want[2]), f
+    assert np.abs(cond_h).max() > 0.001                       # TemporalPreparationProbe.swift:86
+    if not second_order:
+        assert not np.any(flow2_h)                            # :88, the first-order flow is zero
+
+
+def test_large_frame_bit_exact(cuda_op):
+    """One 270x480 frame (the size of benchmark config 3) with flows up to +-40 px."""
+    import torch
+
+    w, h = 480, 270
+    plane = w * h
+    g = np.random.default_rng(9)
+    f16 = lambda a: a.astype(np.float16).astype(np.float32)  # noqa: E731
+    prop, cur, n2 = (f16(g.standard_normal(64 * plane)) for _ in range(3))
+    f1, prev = _flows(plane, 40.0, 1), _flows(plane, 40.0, 2)
+    res = cuda_op.temporal_prepare(w, h, *(torch.from_numpy(a.astype(np.float16)).cuda()
+                                           for a in (prop, cur, n2, f1, prev)), True)
+    torch.cuda.synchronize()
+    want = oracle.temporal_prepare(w, h, prop, cur, n2, f1, prev, True)
+    for got, exp in zip(res, want):
+        assert np.array_equal(got.float().cpu().numpy(), exp)
