@@ -7,16 +7,20 @@
 //                                      warp(feat_n2, flow2), flow1, flow2] (196 channels, the
 //                                      offset network's input) and deform_input = [feat_prop,
 //                                      feat_n2] (the DCN's input).
-// Here it is one kernel over a batch of frames: every thread owns one pixel and a slice of 8 of
-// the 64 feature channels, computes the pixel's second-order flow itself (two bilinear samples of
-// the previous flow, rounded to FP16 as the reference stores it) and then warps its channels of
-// both feature maps with the two flows, so flow2 is never read back.  deform_input is optional:
+// Here it is one kernel over a batch of frames: every thread owns one pixel and a slice of the
+// 64 feature channels, computes the pixel's second-order flow itself (two bilinear samples of the
+// previous flow, rounded to FP16 as the reference stores it) and then warps its channels of both
+// feature maps with the two flows, so flow2 is never read back.  Frames whose channel slices fit
+// in shared memory (Jasna's 64x64 tiles) stage them there first (temporal_prepare_staged_kernel);
+// larger frames gather from global memory (temporal_prepare_kernel).  deform_input is optional:
 // the DCN entry points take the two feature tensors directly (dcn_io.input_second), which makes
 // the concatenation copy unnecessary.  The sampling arithmetic is the reference's (`sample_fp16`,
 // MetalShader.swift:52-74, and the CPU check's `sampleZero`, JasnaCLI.swift:213-225) with one
 // IEEE rounding per operation, so results equal the CPU restatement bit for bit.
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
+
+#include <mutex>
 
 #include "dcn_b200.h"
 #include "dcn_common.cuh"
@@ -129,7 +133,186 @@ __global__ void __launch_bounds__(kTpThreads) temporal_prepare_kernel(const Temp
     }
 }
 
+// ---- frames whose channel slices fit in shared memory ------------------------------
+// Block = (frame, slice of 4 channels).  The block first stages, with coalesced loads, its 4
+// channels of feat_prop and of feat_n2 and both previous-flow channels as channel-interleaved
+// slabs [(H+2)(W+2)] with a one-pixel ring of zeros (8, 8 and 4 bytes per position), writing
+// the feat_current and deform-input copies on the way; then every bilinear corner of 4 channels
+// is one 8-byte shared-memory load instead of four scattered 2-byte global loads.  The sampling
+// arithmetic is the same as above (out-of-slab corners read the zeros the reference reads).
+constexpr int kTsThreads = 256;
+constexpr int kTsSlice = 4;
+constexpr int kTsSlices = kTpChannels / kTsSlice;
+constexpr int kTsBytesPerPosition = 8 + 8;
+constexpr int kTsStage = 4;  // staged positions per thread in flight
+
+struct SlabCorners {
+    int idx;  // top-left corner in the ring-padded slab, valid when in
+    bool in;  // all four corners lie in the padded slab (else every corner is outside the frame)
+    float ly, lx;
+};
+
+__device__ __forceinline__ SlabCorners slab_corners(float y, float x, int H, int W) {
+    const int y0 = __float2int_rd(y), x0 = __float2int_rd(x);
+    SlabCorners c;
+    c.ly = __fsub_rn(y, static_cast<float>(y0));
+    c.lx = __fsub_rn(x, static_cast<float>(x0));
+    c.in = static_cast<unsigned>(y0) + 1u <= static_cast<unsigned>(H) &&
+           static_cast<unsigned>(x0) + 1u <= static_cast<unsigned>(W);
+    c.idx = c.in ? (y0 + 1) * (W + 2) + (x0 + 1) : 0;
+    return c;
+}
+
+__device__ __forceinline__ float bilinear_terms(float v00, float v01, float v10, float v11, float ly, float lx) {
+    const float hy = __fsub_rn(1.0f, ly), hx = __fsub_rn(1.0f, lx);
+    const float t0 = __fmul_rn(__fmul_rn(v00, hy), hx);
+    const float t1 = __fmul_rn(__fmul_rn(v01, hy), lx);
+    const float t2 = __fmul_rn(__fmul_rn(v10, ly), hx);
+    const float t3 = __fmul_rn(__fmul_rn(v11, ly), lx);
+    return __fadd_rn(__fadd_rn(__fadd_rn(t0, t1), t2), t3);
+}
+
+__device__ __forceinline__ float half_of(uint32_t word, int hi) {
+    return __half2float(__ushort_as_half(static_cast<unsigned short>(hi ? word >> 16 : word & 0xffffu)));
+}
+
+__global__ void __launch_bounds__(kTsThreads) temporal_prepare_staged_kernel(const TemporalArgs a) {
+    extern __shared__ __align__(16) uint8_t ts_smem[];
+    const int W = a.W, H = a.H, sw = W + 2;
+    const int positions = (H + 2) * sw;
+    const int64_t plane = static_cast<int64_t>(H) * W;
+    uint2 *prop_s = reinterpret_cast<uint2 *>(ts_smem);
+    uint2 *n2_s = prop_s + positions;
+    const int slice = blockIdx.x % kTsSlices;
+    const int ch0 = slice * kTsSlice;
+    for (int64_t n = blockIdx.x / kTsSlices; n < a.N; n += gridDim.x / kTsSlices) {
+        const int64_t feat = (n * kTpChannels + ch0) * plane;
+        const __half *prop = a.feat_prop + feat, *n2 = a.feat_n2 + feat, *cur = a.feat_current + feat;
+        __half *cond = a.conditions + n * 196 * plane;
+        __half *di = a.deform_input != nullptr ? a.deform_input + n * 128 * plane : nullptr;
+        // Plane copies, 16 bytes per access: feat_current's 4 planes into the conditions, and
+        // feat_prop's and feat_n2's into the deform input (each 4 planes are contiguous).
+        const int64_t vec = (kTsSlice * plane) / 8;  // uint4 per 4 planes (plane % 2 == 0 checked on launch)
+        {
+            const uint4 *cur4 = reinterpret_cast<const uint4 *>(cur);
+            uint4 *cond4 = reinterpret_cast<uint4 *>(cond + (64 + ch0) * plane);
+            for (int64_t i = threadIdx.x; i < vec; i += kTsThreads) cond4[i] = cur4[i];
+            if (di != nullptr) {
+                const uint4 *p4 = reinterpret_cast<const uint4 *>(prop), *n4 = reinterpret_cast<const uint4 *>(n2);
+                uint4 *dp4 = reinterpret_cast<uint4 *>(di + ch0 * plane);
+                uint4 *dn4 = reinterpret_cast<uint4 *>(di + (64 + ch0) * plane);
+                for (int64_t i = threadIdx.x; i < vec; i += kTsThreads) {
+                    dp4[i] = p4[i];
+                    dn4[i] = n4[i];
+                }
+            }
+        }
+        // Stage the slabs (zero ring), kTsStage positions per thread in flight.
+        for (int pos0 = threadIdx.x; pos0 < positions; pos0 += kTsThreads * kTsStage) {
+            unsigned short hp[kTsStage][kTsSlice], hn[kTsStage][kTsSlice];
+            bool inside[kTsStage];
+#pragma unroll
+            for (int u = 0; u < kTsStage; ++u) {
+                const int pos = pos0 + u * kTsThreads;
+                const int py = pos / sw, y = py - 1, x = pos - py * sw - 1;
+                inside[u] = pos < positions && y >= 0 && y < H && x >= 0 && x < W;
+                const int64_t q = inside[u] ? static_cast<int64_t>(y) * W + x : 0;
+#pragma unroll
+                for (int k = 0; k < kTsSlice; ++k) {
+                    hp[u][k] = inside[u] ? __half_as_ushort(prop[k * plane + q]) : 0;
+                    hn[u][k] = inside[u] ? __half_as_ushort(n2[k * plane + q]) : 0;
+                }
+            }
+#pragma unroll
+            for (int u = 0; u < kTsStage; ++u) {
+                const int pos = pos0 + u * kTsThreads;
+                if (pos >= positions) break;
+                prop_s[pos] = make_uint2(hp[u][0] | (static_cast<uint32_t>(hp[u][1]) << 16),
+                                         hp[u][2] | (static_cast<uint32_t>(hp[u][3]) << 16));
+                n2_s[pos] = make_uint2(hn[u][0] | (static_cast<uint32_t>(hn[u][1]) << 16),
+                                       hn[u][2] | (static_cast<uint32_t>(hn[u][3]) << 16));
+            }
+        }
+        __syncthreads();
+        // The second-order flow comes from second_order_flow_kernel, which this kernel follows
+        // as a programmatic dependent: everything above ran while that kernel did.
+        grid_dependency_wait();
+        const __half *f1 = a.flow1 + n * 2 * plane;
+        const __half *f2 = a.flow2 + n * 2 * plane;
+        for (int64_t p = threadIdx.x; p < plane; p += kTsThreads) {
+            const int y = static_cast<int>(p / W), x = static_cast<int>(p - static_cast<int64_t>(y) * W);
+            const float fy = static_cast<float>(y), fx = static_cast<float>(x);
+            const float f1x = __half2float(f1[p]), f1y = __half2float(f1[plane + p]);
+            const float f2x = __half2float(f2[p]), f2y = __half2float(f2[plane + p]);
+            const SlabCorners c1 = slab_corners(__fadd_rn(fy, f1y), __fadd_rn(fx, f1x), H, W);
+            const SlabCorners c2 = slab_corners(__fadd_rn(fy, f2y), __fadd_rn(fx, f2x), H, W);
+#pragma unroll
+            for (int which = 0; which < 2; ++which) {
+                const SlabCorners &c = which ? c2 : c1;
+                const uint2 *s_ = which ? n2_s : prop_s;
+                uint2 q00 = make_uint2(0u, 0u), q01 = q00, q10 = q00, q11 = q00;
+                if (c.in) {
+                    q00 = s_[c.idx];
+                    q01 = s_[c.idx + 1];
+                    q10 = s_[c.idx + sw];
+                    q11 = s_[c.idx + sw + 1];
+                }
+#pragma unroll
+                for (int k = 0; k < kTsSlice; ++k) {
+                    const int wd = k >> 1, hi = k & 1;
+                    const float v = bilinear_terms(half_of(wd ? q00.y : q00.x, hi), half_of(wd ? q01.y : q01.x, hi),
+                                                   half_of(wd ? q10.y : q10.x, hi), half_of(wd ? q11.y : q11.x, hi),
+                                                   c.ly, c.lx);
+                    cond[((which ? 128 : 0) + ch0 + k) * plane + p] = __float2half_rn(v);
+                }
+            }
+        }
+        __syncthreads();  // the slabs are rewritten for the next frame
+    }
+}
+
+// First pass of the staged form: per pixel the second-order flow (accumulate_second_order_flow_fp16)
+// and the four flow channels of the conditions.  The staged kernel is its programmatic dependent.
+__global__ void __launch_bounds__(kTsThreads) second_order_flow_kernel(const TemporalArgs a) {
+    allow_dependent_launch();
+    const int64_t plane = static_cast<int64_t>(a.H) * a.W;
+    const int64_t i = static_cast<int64_t>(blockIdx.x) * kTsThreads + threadIdx.x;
+    if (i >= plane * a.N) return;
+    const int64_t n = i / plane, p = i - n * plane;
+    const int y = static_cast<int>(p / a.W), x = static_cast<int>(p - static_cast<int64_t>(y) * a.W);
+    const __half *f1 = a.flow1 + n * 2 * plane;
+    const float f1x = __half2float(f1[p]), f1y = __half2float(f1[plane + p]);
+    float f2x = 0.0f, f2y = 0.0f;
+    if (a.has_second_order) {
+        const Corners c1 = corners(__fadd_rn(static_cast<float>(y), f1y), __fadd_rn(static_cast<float>(x), f1x),
+                                   a.H, a.W);
+        const __half *prev = a.previous + n * 2 * plane;
+        f2x = round_f16(__fadd_rn(f1x, sample(prev, c1, a.W)));
+        f2y = round_f16(__fadd_rn(f1y, sample(prev + plane, c1, a.W)));
+    }
+    __half *f2 = a.flow2 + n * 2 * plane;
+    __half *cond = a.conditions + n * 196 * plane;
+    f2[p] = __float2half_rn(f2x);
+    f2[plane + p] = __float2half_rn(f2y);
+    cond[192 * plane + p] = f1[p];
+    cond[193 * plane + p] = f1[plane + p];
+    cond[194 * plane + p] = __float2half_rn(f2x);
+    cond[195 * plane + p] = __float2half_rn(f2y);
+}
+
 }  // namespace
+
+// Shared memory of the staged kernel for a frame, or 0 when its slabs do not fit two blocks
+// per SM.
+size_t temporal_staged_smem(int height, int width) {
+    const size_t bytes = static_cast<size_t>(height + 2) * (width + 2) * kTsBytesPerPosition;
+    return bytes <= 110 * 1024 ? bytes : 0;
+}
+
+cudaError_t temporal_prepare_device() {
+    return cudaFuncSetAttribute(temporal_prepare_staged_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                110 * 1024);
+}
 
 cudaError_t launch_temporal_prepare(int n, int height, int width, const __half *feat_prop, const __half *feat_current,
                                     const __half *feat_n2, const __half *flow1, const __half *previous,
@@ -137,6 +320,25 @@ cudaError_t launch_temporal_prepare(int n, int height, int width, const __half *
                                     cudaStream_t stream) {
     TemporalArgs a{feat_prop, feat_current, feat_n2, flow1, previous, conditions, deform_input, flow2,
                    n, height, width, has_second_order ? 1 : 0};
+    const size_t smem = temporal_staged_smem(height, width);
+    const bool vec_ok = (static_cast<int64_t>(height) * width) % 2 == 0 &&
+                        ((reinterpret_cast<uintptr_t>(feat_prop) | reinterpret_cast<uintptr_t>(feat_current) |
+                          reinterpret_cast<uintptr_t>(feat_n2) | reinterpret_cast<uintptr_t>(conditions) |
+                          reinterpret_cast<uintptr_t>(deform_input)) & 15u) == 0;
+    if (smem > 0 && vec_ok) {
+        static std::once_flag once;
+        static cudaError_t set = cudaSuccess;
+        std::call_once(once, [] { set = temporal_prepare_device(); });
+        if (set != cudaSuccess) return set;
+        const int64_t pixels = static_cast<int64_t>(n) * height * width;
+        second_order_flow_kernel<<<static_cast<unsigned>((pixels + kTsThreads - 1) / kTsThreads), kTsThreads, 0,
+                                   stream>>>(a);
+        cudaError_t e = cudaGetLastError();
+        if (e != cudaSuccess) return e;
+        const int64_t blocks = static_cast<int64_t>(n) * kTsSlices;
+        const unsigned grid = static_cast<unsigned>(blocks < 65535LL * kTsSlices ? blocks : 65535LL * kTsSlices);
+        return launch_dependent(temporal_prepare_staged_kernel, dim3(grid), dim3(kTsThreads), smem, stream, a);
+    }
     const int64_t plane = static_cast<int64_t>(height) * width;
     const dim3 grid(static_cast<unsigned>((plane + kTpThreads - 1) / kTpThreads), kTpSlices,
                     static_cast<unsigned>(n < 65535 ? n : 65535));
