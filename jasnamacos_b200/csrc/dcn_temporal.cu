@@ -145,6 +145,7 @@ constexpr int kTsSlice = 4;
 constexpr int kTsSlices = kTpChannels / kTsSlice;
 constexpr int kTsBytesPerPosition = 8 + 8;
 constexpr int kTsStage = 4;  // staged positions per thread in flight
+static_assert(kTsSlice == 4, "the staged kernel's gathers hold 4 channels per 8-byte position");
 
 struct SlabCorners {
     int idx;  // top-left corner in the ring-padded slab, valid when in
@@ -172,55 +173,70 @@ __device__ __forceinline__ float bilinear_terms(float v00, float v01, float v10,
     return __fadd_rn(__fadd_rn(__fadd_rn(t0, t1), t2), t3);
 }
 
-__device__ __forceinline__ float half_of(uint32_t word, int hi) {
-    return __half2float(__ushort_as_half(static_cast<unsigned short>(hi ? word >> 16 : word & 0xffffu)));
+__device__ __forceinline__ float2 pair_to_float2(uint32_t word) {
+    __half2 h;
+    memcpy(&h, &word, sizeof(h));
+    return __half22float2(h);
 }
 
 __global__ void __launch_bounds__(kTsThreads) temporal_prepare_staged_kernel(const TemporalArgs a) {
     extern __shared__ __align__(16) uint8_t ts_smem[];
+    // In-frame offsets are 32-bit (a staged frame holds at most a few thousand pixels); rows and
+    // columns advance incrementally with the thread stride instead of by division.
     const int W = a.W, H = a.H, sw = W + 2;
     const int positions = (H + 2) * sw;
-    const int64_t plane = static_cast<int64_t>(H) * W;
+    const int plane = H * W;
     uint2 *prop_s = reinterpret_cast<uint2 *>(ts_smem);
     uint2 *n2_s = prop_s + positions;
     const int slice = blockIdx.x % kTsSlices;
     const int ch0 = slice * kTsSlice;
+    const int step_y = kTsThreads / W, step_x = kTsThreads % W;           // pixel stride as (rows, cols)
+    const int pstep_y = kTsThreads / sw, pstep_x = kTsThreads % sw;       // padded-position stride
+    const int y_first = static_cast<int>(threadIdx.x) / W, x_first = static_cast<int>(threadIdx.x) % W;
+    const int py_first = static_cast<int>(threadIdx.x) / sw, px_first = static_cast<int>(threadIdx.x) % sw;
     for (int64_t n = blockIdx.x / kTsSlices; n < a.N; n += gridDim.x / kTsSlices) {
         const int64_t feat = (n * kTpChannels + ch0) * plane;
         const __half *prop = a.feat_prop + feat, *n2 = a.feat_n2 + feat, *cur = a.feat_current + feat;
-        __half *cond = a.conditions + n * 196 * plane;
-        __half *di = a.deform_input != nullptr ? a.deform_input + n * 128 * plane : nullptr;
+        __half *cond = a.conditions + n * 196 * static_cast<int64_t>(plane);
+        __half *di = a.deform_input != nullptr ? a.deform_input + n * 128 * static_cast<int64_t>(plane) : nullptr;
         // Plane copies, 16 bytes per access: feat_current's 4 planes into the conditions, and
         // feat_prop's and feat_n2's into the deform input (each 4 planes are contiguous).
-        const int64_t vec = (kTsSlice * plane) / 8;  // uint4 per 4 planes (plane % 2 == 0 checked on launch)
+        const int vec = (kTsSlice * plane) / 8;  // uint4 per 4 planes (plane % 2 == 0 checked on launch)
         {
             const uint4 *cur4 = reinterpret_cast<const uint4 *>(cur);
             uint4 *cond4 = reinterpret_cast<uint4 *>(cond + (64 + ch0) * plane);
-            for (int64_t i = threadIdx.x; i < vec; i += kTsThreads) cond4[i] = cur4[i];
+            for (int i = threadIdx.x; i < vec; i += kTsThreads) cond4[i] = cur4[i];
             if (di != nullptr) {
                 const uint4 *p4 = reinterpret_cast<const uint4 *>(prop), *n4 = reinterpret_cast<const uint4 *>(n2);
                 uint4 *dp4 = reinterpret_cast<uint4 *>(di + ch0 * plane);
                 uint4 *dn4 = reinterpret_cast<uint4 *>(di + (64 + ch0) * plane);
-                for (int64_t i = threadIdx.x; i < vec; i += kTsThreads) {
+                for (int i = threadIdx.x; i < vec; i += kTsThreads) {
                     dp4[i] = p4[i];
                     dn4[i] = n4[i];
                 }
             }
         }
         // Stage the slabs (zero ring), kTsStage positions per thread in flight.
+        int spy = py_first, spx = px_first;  // padded row/column of this thread's next position
         for (int pos0 = threadIdx.x; pos0 < positions; pos0 += kTsThreads * kTsStage) {
             unsigned short hp[kTsStage][kTsSlice], hn[kTsStage][kTsSlice];
             bool inside[kTsStage];
 #pragma unroll
             for (int u = 0; u < kTsStage; ++u) {
                 const int pos = pos0 + u * kTsThreads;
-                const int py = pos / sw, y = py - 1, x = pos - py * sw - 1;
+                const int y = spy - 1, x = spx - 1;
                 inside[u] = pos < positions && y >= 0 && y < H && x >= 0 && x < W;
-                const int64_t q = inside[u] ? static_cast<int64_t>(y) * W + x : 0;
+                const int q = inside[u] ? y * W + x : 0;
 #pragma unroll
                 for (int k = 0; k < kTsSlice; ++k) {
                     hp[u][k] = inside[u] ? __half_as_ushort(prop[k * plane + q]) : 0;
                     hn[u][k] = inside[u] ? __half_as_ushort(n2[k * plane + q]) : 0;
+                }
+                spy += pstep_y;
+                spx += pstep_x;
+                if (spx >= sw) {
+                    spx -= sw;
+                    ++spy;
                 }
             }
 #pragma unroll
@@ -237,10 +253,11 @@ __global__ void __launch_bounds__(kTsThreads) temporal_prepare_staged_kernel(con
         // The second-order flow comes from second_order_flow_kernel, which this kernel follows
         // as a programmatic dependent: everything above ran while that kernel did.
         grid_dependency_wait();
-        const __half *f1 = a.flow1 + n * 2 * plane;
-        const __half *f2 = a.flow2 + n * 2 * plane;
-        for (int64_t p = threadIdx.x; p < plane; p += kTsThreads) {
-            const int y = static_cast<int>(p / W), x = static_cast<int>(p - static_cast<int64_t>(y) * W);
+        const __half *f1 = a.flow1 + n * 2 * static_cast<int64_t>(plane);
+        const __half *f2 = a.flow2 + n * 2 * static_cast<int64_t>(plane);
+        __half *out_prop = cond + ch0 * plane, *out_n2 = cond + (128 + ch0) * plane;
+        int y = y_first, x = x_first;
+        for (int p = threadIdx.x; p < plane; p += kTsThreads) {
             const float fy = static_cast<float>(y), fx = static_cast<float>(x);
             const float f1x = __half2float(f1[p]), f1y = __half2float(f1[plane + p]);
             const float f2x = __half2float(f2[p]), f2y = __half2float(f2[plane + p]);
@@ -250,6 +267,7 @@ __global__ void __launch_bounds__(kTsThreads) temporal_prepare_staged_kernel(con
             for (int which = 0; which < 2; ++which) {
                 const SlabCorners &c = which ? c2 : c1;
                 const uint2 *s_ = which ? n2_s : prop_s;
+                __half *o = (which ? out_n2 : out_prop) + p;
                 uint2 q00 = make_uint2(0u, 0u), q01 = q00, q10 = q00, q11 = q00;
                 if (c.in) {
                     q00 = s_[c.idx];
@@ -257,14 +275,21 @@ __global__ void __launch_bounds__(kTsThreads) temporal_prepare_staged_kernel(con
                     q10 = s_[c.idx + sw];
                     q11 = s_[c.idx + sw + 1];
                 }
-#pragma unroll
-                for (int k = 0; k < kTsSlice; ++k) {
-                    const int wd = k >> 1, hi = k & 1;
-                    const float v = bilinear_terms(half_of(wd ? q00.y : q00.x, hi), half_of(wd ? q01.y : q01.x, hi),
-                                                   half_of(wd ? q10.y : q10.x, hi), half_of(wd ? q11.y : q11.x, hi),
-                                                   c.ly, c.lx);
-                    cond[((which ? 128 : 0) + ch0 + k) * plane + p] = __float2half_rn(v);
-                }
+                // Each 32-bit word holds two channels: one paired conversion per word.
+                const float2 a00 = pair_to_float2(q00.x), b00 = pair_to_float2(q00.y);
+                const float2 a01 = pair_to_float2(q01.x), b01 = pair_to_float2(q01.y);
+                const float2 a10 = pair_to_float2(q10.x), b10 = pair_to_float2(q10.y);
+                const float2 a11 = pair_to_float2(q11.x), b11 = pair_to_float2(q11.y);
+                o[0] = __float2half_rn(bilinear_terms(a00.x, a01.x, a10.x, a11.x, c.ly, c.lx));
+                o[plane] = __float2half_rn(bilinear_terms(a00.y, a01.y, a10.y, a11.y, c.ly, c.lx));
+                o[2 * plane] = __float2half_rn(bilinear_terms(b00.x, b01.x, b10.x, b11.x, c.ly, c.lx));
+                o[3 * plane] = __float2half_rn(bilinear_terms(b00.y, b01.y, b10.y, b11.y, c.ly, c.lx));
+            }
+            y += step_y;
+            x += step_x;
+            if (x >= W) {
+                x -= W;
+                ++y;
             }
         }
         __syncthreads();  // the slabs are rewritten for the next frame
