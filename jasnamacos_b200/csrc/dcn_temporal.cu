@@ -257,10 +257,20 @@ __global__ void __launch_bounds__(kTsThreads) temporal_prepare_staged_kernel(con
         const __half *f2 = a.flow2 + n * 2 * static_cast<int64_t>(plane);
         __half *out_prop = cond + ch0 * plane, *out_n2 = cond + (128 + ch0) * plane;
         int y = y_first, x = x_first;
+        // The four flow values of the next pixel are loaded one iteration ahead.
+        __half n1x = __float2half_rn(0.0f), n1y = n1x, n2x = n1x, n2y = n1x;
+        if (static_cast<int>(threadIdx.x) < plane) {
+            n1x = f1[threadIdx.x], n1y = f1[plane + threadIdx.x];
+            n2x = f2[threadIdx.x], n2y = f2[plane + threadIdx.x];
+        }
         for (int p = threadIdx.x; p < plane; p += kTsThreads) {
             const float fy = static_cast<float>(y), fx = static_cast<float>(x);
-            const float f1x = __half2float(f1[p]), f1y = __half2float(f1[plane + p]);
-            const float f2x = __half2float(f2[p]), f2y = __half2float(f2[plane + p]);
+            const float f1x = __half2float(n1x), f1y = __half2float(n1y);
+            const float f2x = __half2float(n2x), f2y = __half2float(n2y);
+            if (p + kTsThreads < plane) {
+                n1x = f1[p + kTsThreads], n1y = f1[plane + p + kTsThreads];
+                n2x = f2[p + kTsThreads], n2y = f2[plane + p + kTsThreads];
+            }
             const SlabCorners c1 = slab_corners(__fadd_rn(fy, f1y), __fadd_rn(fx, f1x), H, W);
             const SlabCorners c2 = slab_corners(__fadd_rn(fy, f2y), __fadd_rn(fx, f2x), H, W);
 #pragma unroll
