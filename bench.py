@@ -391,6 +391,28 @@ def temporal_section(op, dev, frames: int, steps: int, peaks: dict) -> dict:
         key = "with_deform_input" if with_di else "without_deform_input"
         out[key] = {"ms": ms, "Mpx_s": frames * plane / (ms * 1e-3) / 1e6, "GB_s": gbs,
                     "frac_hbm": gbs / peaks["hbm_gbs"], "algorithmic_bytes_per_px": bytes_px}
+    # The reference's own timing of this step (TemporalPreparationProbe.swift:33-49; README:509-515):
+    # one frame per call, the backward and then the forward direction, timed together.
+    def frame(t, c, f):
+        return t[f * c * plane:(f + 1) * c * plane]
+
+    def pair():
+        for f in (0, 1):
+            op.temporal_prepare(w, h, frame(feats[0], 64, f), frame(feats[1], 64, f), frame(feats[2], 64, f),
+                                frame(flows[0], 2, f), frame(flows[1], 2, f), True, batch=1,
+                                conditions=frame(cond, 196, f), deform_input=frame(di, 128, f),
+                                flow2=frame(flow2, 2, f))
+
+    if frames >= 2:
+        replay = graphed(pair, True)
+        for _ in range(3):
+            replay()
+        torch.cuda.synchronize(dev)
+        out["probe_pair"] = {
+            "ms": event_time_ms(replay, 50) / 50,
+            "what": "two single-frame calls (backward and forward directions, deform input included) per step, "
+                    "as the reference's temporal probe times them; CUDA-graph replays. The reference publishes "
+                    "0.284-0.289 ms median for this on an M4 GPU (Metal, not measurable here)"}
     run(True)()
     torch.cuda.synchronize(dev)
     mismatches, compared = 0, 0
