@@ -103,3 +103,51 @@ def test_large_frame_bit_exact(cuda_op):
     want = oracle.temporal_prepare(w, h, prop, cur, n2, f1, prev, True)
     for got, exp in zip(res, want):
         assert np.array_equal(got.float().cpu().numpy(), exp)
+
+
+def test_chain_into_the_raw_form_dcn(cuda_op, host_threads):
+    """The alignment step as the reference chains it (S/FusedFourPassRecurrenceProbe.swift:609-630):
+    the temporal preparation's flow1/flow2 and deform input feed the raw-form DCN (offset transform
+    fused).  The DCN reading the concatenated deform input and the DCN reading feat_prop and feat_n2
+    as two tensors (dcn_io, no concatenation) give the same bits; both match the CPU chain
+    (oracle temporal preparation -> oracle offset transform -> oracle DCN) under the FP16 gates."""
+    import torch
+
+    from jasnamacos_b200 import synthetic
+    from jasnamacos_b200.deform_conv import DeformConvShape
+
+    w = h = 64
+    plane = w * h
+    frames = 2
+    shape = DeformConvShape.jasna_propagation(frames, h, w)
+    g = np.random.default_rng(31)
+    f16 = lambda a: a.astype(np.float16).astype(np.float32)  # noqa: E731
+    prop, cur, n2 = (f16(g.standard_normal(frames * 64 * plane)) for _ in range(3))
+    f1, prev = _flows(frames * plane, 8.0, 3), _flows(frames * plane, 8.0, 4)
+    raw = f16(g.standard_normal(frames * 432 * plane))
+    wt, b = synthetic.weights(shape, 5)
+    wt, b = f16(wt), f16(b)
+    dev = lambda a: torch.from_numpy(a.astype(np.float16)).cuda()  # noqa: E731
+    prop_d, n2_d = dev(prop), dev(n2)
+    cond, di, flow2 = cuda_op.temporal_prepare(w, h, prop_d, dev(cur), n2_d, dev(f1), dev(prev), True, batch=frames)
+    packed = cuda_op.prepack(shape, dev(wt))
+    flag = torch.zeros(1, dtype=torch.int32, device="cuda")
+    concat = cuda_op.forward_f16_raw(shape, di, dev(raw), dev(f1), flow2, packed, dev(b), flag=flag)
+    # two tensors, per image [64][H][W] each: the DCN input split at channel 64
+    split = cuda_op.forward_f16_raw(shape, prop_d, dev(raw), dev(f1), flow2, packed, dev(b), flag=flag,
+                                    input_second=n2_d)
+    torch.cuda.synchronize()
+    cuda_op.device_error()
+    assert int(flag.item()) == 0
+    assert torch.equal(concat, split)
+    got = concat.float().cpu().numpy()
+    for f in range(frames):
+        sl = lambda a, c: a[f * c * plane:(f + 1) * c * plane]  # noqa: E731
+        _, di_ref, flow2_ref = oracle.temporal_prepare(w, h, sl(prop, 64), sl(cur, 64), sl(n2, 64), sl(f1, 2),
+                                                       sl(prev, 2), True)
+        assert np.array_equal(flow2[f * 2 * plane:(f + 1) * 2 * plane].float().cpu().numpy(), flow2_ref)
+        off, msk = oracle.prepare_offsets(plane, sl(raw, 432), sl(f1, 2), flow2_ref)
+        one = shape.with_batch(1)
+        ref = oracle.run(one, di_ref, f16(off), f16(msk), wt, b, threads=host_threads)
+        d = np.abs(got[f * one.output_count:(f + 1) * one.output_count] - ref)
+        assert d.max() <= 2e-2 and d.mean() <= 2e-3, (f, float(d.max()), float(d.mean()))
