@@ -134,12 +134,16 @@ __global__ void __launch_bounds__(kTpThreads) temporal_prepare_kernel(const Temp
 }
 
 // ---- frames whose channel slices fit in shared memory ------------------------------
-// Block = (frame, slice of 4 channels).  The block first stages, with coalesced loads, its 4
-// channels of feat_prop and of feat_n2 and both previous-flow channels as channel-interleaved
-// slabs [(H+2)(W+2)] with a one-pixel ring of zeros (8, 8 and 4 bytes per position), writing
-// the feat_current and deform-input copies on the way; then every bilinear corner of 4 channels
-// is one 8-byte shared-memory load instead of four scattered 2-byte global loads.  The sampling
-// arithmetic is the same as above (out-of-slab corners read the zeros the reference reads).
+// Two launches.  second_order_flow_kernel computes every pixel's second-order flow once per frame
+// (with the global-memory sampling above) and writes it and the four flow channels of the
+// conditions.  temporal_prepare_staged_kernel, its programmatic dependent, runs one block per
+// (frame, slice of 4 channels): it copies its 4 planes of feat_current into the conditions and
+// of feat_prop / feat_n2 into the deform input with 16-byte accesses, stages its 4 channels of
+// feat_prop and of feat_n2 as channel-interleaved slabs [(H+2)(W+2)] with a one-pixel ring of
+// zeros (8 bytes per position each), and only then waits for the flows; every bilinear corner of
+// 4 channels is then one 8-byte shared-memory load instead of four scattered 2-byte global loads.
+// The sampling arithmetic is the same as above (out-of-slab corners read the zeros the reference
+// reads), so both forms give the same bits.
 constexpr int kTsThreads = 256;
 constexpr int kTsSlice = 4;
 constexpr int kTsSlices = kTpChannels / kTsSlice;
@@ -337,8 +341,8 @@ __global__ void __launch_bounds__(kTsThreads) second_order_flow_kernel(const Tem
 
 }  // namespace
 
-// Shared memory of the staged kernel for a frame, or 0 when its slabs do not fit two blocks
-// per SM.
+// Shared memory of the staged kernel for a frame (two slabs), or 0 when they exceed 110 KB, which
+// keeps at least two blocks per SM (a 64x64 frame takes 69.7 KB: three).
 size_t temporal_staged_smem(int height, int width) {
     const size_t bytes = static_cast<size_t>(height + 2) * (width + 2) * kTsBytesPerPosition;
     return bytes <= 110 * 1024 ? bytes : 0;
