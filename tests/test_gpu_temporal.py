@@ -151,3 +151,30 @@ def test_chain_into_the_raw_form_dcn(cuda_op, host_threads):
         ref = oracle.run(one, di_ref, f16(off), f16(msk), wt, b, threads=host_threads)
         d = np.abs(got[f * one.output_count:(f + 1) * one.output_count] - ref)
         assert d.max() <= 2e-2 and d.mean() <= 2e-3, (f, float(d.max()), float(d.mean()))
+
+
+@pytest.mark.parametrize("w,h", [(44, 30), (70, 50), (300, 20), (17, 13)],
+                         ids=["44x30", "70x50", "300x20_wide", "17x13_odd_plane"])
+def test_irregular_frames_bit_exact(cuda_op, w, h):
+    """Frame sizes whose width does not divide the staged kernel's 256-thread stride (its rows and
+    columns advance by stepping, not division), one wider than 256 pixels, and an odd pixel count
+    (which takes the global-memory form): three frames each, against the oracle."""
+    import torch
+
+    plane = w * h
+    frames = 3
+    g = np.random.default_rng(w * 1000 + h)
+    f16 = lambda a: a.astype(np.float16).astype(np.float32)  # noqa: E731
+    prop, cur, n2 = (f16(g.standard_normal(frames * 64 * plane)) for _ in range(3))
+    f1, prev = _flows(frames * plane, 12.0, w), _flows(frames * plane, 12.0, h)
+    dev = lambda a: torch.from_numpy(a.astype(np.float16)).cuda()  # noqa: E731
+    cond, di, flow2 = cuda_op.temporal_prepare(w, h, dev(prop), dev(cur), dev(n2), dev(f1), dev(prev), True,
+                                               batch=frames)
+    torch.cuda.synchronize()
+    cuda_op.device_error()
+    got = [t.float().cpu().numpy() for t in (cond, di, flow2)]
+    for f in range(frames):
+        sl = lambda a, c: a[f * c * plane:(f + 1) * c * plane]  # noqa: E731
+        want = oracle.temporal_prepare(w, h, sl(prop, 64), sl(cur, 64), sl(n2, 64), sl(f1, 2), sl(prev, 2), True)
+        for a, b, c in zip(got, want, (196, 128, 2)):
+            assert np.array_equal(sl(a, c), b), (w, h, f, c)
