@@ -56,6 +56,7 @@ void slab_plan(const Params &p, int sm_count, dcn_plan *out);
 size_t slab_workspace_bytes(const Params &p);
 size_t slab_packed_weight_bytes(const Params &p);
 cudaError_t slab_prepare_device();
+cudaError_t temporal_prepare_device();
 cudaError_t launch_regroup_slabs(const Params &p, const SplitInput<__half> &input, void *workspace,
                                  cudaStream_t stream);
 cudaError_t launch_prepack_slab(const Params &p, const void *src, dcn_dtype src_dtype, int layout, void *dst,
@@ -144,6 +145,7 @@ dcn_status current_device(DeviceInfo **out) {
         if (d.sm100) {
             e = fused_prepare_device(&d.err_word);
             if (e == cudaSuccess) e = slab_prepare_device();
+            if (e == cudaSuccess) e = temporal_prepare_device();
             if (e != cudaSuccess) {
                 cudaGetLastError();
                 return from_cuda(e);

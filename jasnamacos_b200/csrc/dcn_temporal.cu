@@ -20,8 +20,6 @@
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
-#include <mutex>
-
 #include "dcn_b200.h"
 #include "dcn_common.cuh"
 
@@ -348,6 +346,8 @@ size_t temporal_staged_smem(int height, int width) {
     return bytes <= 110 * 1024 ? bytes : 0;
 }
 
+// The staged kernel's opt-in to more than 48 KB of dynamic shared memory, a per-device (and
+// per-context) function attribute.
 cudaError_t temporal_prepare_device() {
     return cudaFuncSetAttribute(temporal_prepare_staged_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                 110 * 1024);
@@ -365,10 +365,8 @@ cudaError_t launch_temporal_prepare(int n, int height, int width, const __half *
                           reinterpret_cast<uintptr_t>(feat_n2) | reinterpret_cast<uintptr_t>(conditions) |
                           reinterpret_cast<uintptr_t>(deform_input)) & 15u) == 0;
     if (smem > 0 && vec_ok) {
-        static std::once_flag once;
-        static cudaError_t set = cudaSuccess;
-        std::call_once(once, [] { set = temporal_prepare_device(); });
-        if (set != cudaSuccess) return set;
+        // The shared-memory opt-in was made by temporal_prepare_device, which the C entry's device
+        // set-up (current_device in dcn_api.cu) runs once per device and context.
         const int64_t pixels = static_cast<int64_t>(n) * height * width;
         second_order_flow_kernel<<<static_cast<unsigned>((pixels + kTsThreads - 1) / kTsThreads), kTsThreads, 0,
                                    stream>>>(a);
