@@ -265,6 +265,7 @@ __global__ void __launch_bounds__(kTsThreads) temporal_prepare_staged_kernel(con
             n1x = f1[threadIdx.x], n1y = f1[plane + threadIdx.x];
             n2x = f2[threadIdx.x], n2y = f2[plane + threadIdx.x];
         }
+#pragma unroll 2
         for (int p = threadIdx.x; p < plane; p += kTsThreads) {
             const float fy = static_cast<float>(y), fx = static_cast<float>(x);
             const float f1x = __half2float(n1x), f1y = __half2float(n1y);
