@@ -135,17 +135,18 @@ __global__ void __launch_bounds__(kTpThreads) temporal_prepare_kernel(const Temp
 // Two launches.  second_order_flow_kernel computes every pixel's second-order flow once per frame
 // (with the global-memory sampling above) and writes it and the four flow channels of the
 // conditions.  temporal_prepare_staged_kernel, its programmatic dependent, runs one block per
-// (frame, slice of 4 channels): it copies its 4 planes of feat_current into the conditions and
-// of feat_prop / feat_n2 into the deform input with 16-byte accesses, stages its 4 channels of
-// feat_prop and of feat_n2 as channel-interleaved slabs [(H+2)(W+2)] with a one-pixel ring of
-// zeros (8 bytes per position each), and only then waits for the flows; every bilinear corner of
-// 4 channels is then one 8-byte shared-memory load instead of four scattered 2-byte global loads.
+// (frame, map, slice of 4 channels), map 0 warping feat_prop by flow1 and map 1 feat_n2 by flow2:
+// it copies its 4 planes into the deform input (and, for map 0, feat_current's into the
+// conditions) with 16-byte accesses, stages its 4 channels as a channel-interleaved slab
+// [(H+2)(W+2)] with a one-pixel ring of zeros (8 bytes per position), and (map 1 only) then waits
+// for the second-order flow; every bilinear corner of 4 channels is then one 8-byte shared-memory
+// load instead of four scattered 2-byte global loads.
 // The sampling arithmetic is the same as above (out-of-slab corners read the zeros the reference
 // reads), so both forms give the same bits.
 constexpr int kTsThreads = 256;
 constexpr int kTsSlice = 4;
 constexpr int kTsSlices = kTpChannels / kTsSlice;
-constexpr int kTsBytesPerPosition = 8 + 8;
+constexpr int kTsBytesPerPosition = 8;
 constexpr int kTsStage = 4;  // staged positions per thread in flight
 static_assert(kTsSlice == 4, "the staged kernel's gathers hold 4 channels per 8-byte position");
 
@@ -188,52 +189,48 @@ __global__ void __launch_bounds__(kTsThreads) temporal_prepare_staged_kernel(con
     const int W = a.W, H = a.H, sw = W + 2;
     const int positions = (H + 2) * sw;
     const int plane = H * W;
-    uint2 *prop_s = reinterpret_cast<uint2 *>(ts_smem);
-    uint2 *n2_s = prop_s + positions;
-    const int slice = blockIdx.x % kTsSlices;
-    const int ch0 = slice * kTsSlice;
+    uint2 *slab_s = reinterpret_cast<uint2 *>(ts_smem);
+    // Block = (frame, map, 4-channel slice): map 0 warps feat_prop by flow1 (and copies
+    // feat_current), map 1 warps feat_n2 by flow2; the two share no data.
+    const int job = blockIdx.x % (2 * kTsSlices);
+    const int map = job / kTsSlices;
+    const int ch0 = (job % kTsSlices) * kTsSlice;
     const int step_y = kTsThreads / W, step_x = kTsThreads % W;           // pixel stride as (rows, cols)
     const int pstep_y = kTsThreads / sw, pstep_x = kTsThreads % sw;       // padded-position stride
     const int y_first = static_cast<int>(threadIdx.x) / W, x_first = static_cast<int>(threadIdx.x) % W;
     const int py_first = static_cast<int>(threadIdx.x) / sw, px_first = static_cast<int>(threadIdx.x) % sw;
-    for (int64_t n = blockIdx.x / kTsSlices; n < a.N; n += gridDim.x / kTsSlices) {
+    for (int64_t n = blockIdx.x / (2 * kTsSlices); n < a.N; n += gridDim.x / (2 * kTsSlices)) {
         const int64_t feat = (n * kTpChannels + ch0) * plane;
-        const __half *prop = a.feat_prop + feat, *n2 = a.feat_n2 + feat, *cur = a.feat_current + feat;
+        const __half *src = (map ? a.feat_n2 : a.feat_prop) + feat;
         __half *cond = a.conditions + n * 196 * static_cast<int64_t>(plane);
         __half *di = a.deform_input != nullptr ? a.deform_input + n * 128 * static_cast<int64_t>(plane) : nullptr;
-        // Plane copies, 16 bytes per access: feat_current's 4 planes into the conditions, and
-        // feat_prop's and feat_n2's into the deform input (each 4 planes are contiguous).
+        // Plane copies, 16 bytes per access: feat_current's 4 planes into the conditions (map 0),
+        // and the map's 4 planes into the deform input (each 4 planes are contiguous).
         const int vec = (kTsSlice * plane) / 8;  // uint4 per 4 planes (plane % 2 == 0 checked on launch)
         {
-            const uint4 *cur4 = reinterpret_cast<const uint4 *>(cur);
-            uint4 *cond4 = reinterpret_cast<uint4 *>(cond + (64 + ch0) * plane);
-            for (int i = threadIdx.x; i < vec; i += kTsThreads) cond4[i] = cur4[i];
+            if (map == 0) {
+                const uint4 *cur4 = reinterpret_cast<const uint4 *>(a.feat_current + feat);
+                uint4 *cond4 = reinterpret_cast<uint4 *>(cond + (64 + ch0) * plane);
+                for (int i = threadIdx.x; i < vec; i += kTsThreads) cond4[i] = cur4[i];
+            }
             if (di != nullptr) {
-                const uint4 *p4 = reinterpret_cast<const uint4 *>(prop), *n4 = reinterpret_cast<const uint4 *>(n2);
-                uint4 *dp4 = reinterpret_cast<uint4 *>(di + ch0 * plane);
-                uint4 *dn4 = reinterpret_cast<uint4 *>(di + (64 + ch0) * plane);
-                for (int i = threadIdx.x; i < vec; i += kTsThreads) {
-                    dp4[i] = p4[i];
-                    dn4[i] = n4[i];
-                }
+                const uint4 *s4 = reinterpret_cast<const uint4 *>(src);
+                uint4 *d4 = reinterpret_cast<uint4 *>(di + (64 * map + ch0) * plane);
+                for (int i = threadIdx.x; i < vec; i += kTsThreads) d4[i] = s4[i];
             }
         }
-        // Stage the slabs (zero ring), kTsStage positions per thread in flight.
+        // Stage the slab (zero ring), kTsStage positions per thread in flight.
         int spy = py_first, spx = px_first;  // padded row/column of this thread's next position
         for (int pos0 = threadIdx.x; pos0 < positions; pos0 += kTsThreads * kTsStage) {
-            unsigned short hp[kTsStage][kTsSlice], hn[kTsStage][kTsSlice];
-            bool inside[kTsStage];
+            unsigned short hv[kTsStage][kTsSlice];
 #pragma unroll
             for (int u = 0; u < kTsStage; ++u) {
                 const int pos = pos0 + u * kTsThreads;
                 const int y = spy - 1, x = spx - 1;
-                inside[u] = pos < positions && y >= 0 && y < H && x >= 0 && x < W;
-                const int q = inside[u] ? y * W + x : 0;
+                const bool inside = pos < positions && y >= 0 && y < H && x >= 0 && x < W;
+                const int q = inside ? y * W + x : 0;
 #pragma unroll
-                for (int k = 0; k < kTsSlice; ++k) {
-                    hp[u][k] = inside[u] ? __half_as_ushort(prop[k * plane + q]) : 0;
-                    hn[u][k] = inside[u] ? __half_as_ushort(n2[k * plane + q]) : 0;
-                }
+                for (int k = 0; k < kTsSlice; ++k) hv[u][k] = inside ? __half_as_ushort(src[k * plane + q]) : 0;
                 spy += pstep_y;
                 spx += pstep_x;
                 if (spx >= sw) {
@@ -245,59 +242,51 @@ __global__ void __launch_bounds__(kTsThreads) temporal_prepare_staged_kernel(con
             for (int u = 0; u < kTsStage; ++u) {
                 const int pos = pos0 + u * kTsThreads;
                 if (pos >= positions) break;
-                prop_s[pos] = make_uint2(hp[u][0] | (static_cast<uint32_t>(hp[u][1]) << 16),
-                                         hp[u][2] | (static_cast<uint32_t>(hp[u][3]) << 16));
-                n2_s[pos] = make_uint2(hn[u][0] | (static_cast<uint32_t>(hn[u][1]) << 16),
-                                       hn[u][2] | (static_cast<uint32_t>(hn[u][3]) << 16));
+                slab_s[pos] = make_uint2(hv[u][0] | (static_cast<uint32_t>(hv[u][1]) << 16),
+                                         hv[u][2] | (static_cast<uint32_t>(hv[u][3]) << 16));
             }
         }
         __syncthreads();
-        // The second-order flow comes from second_order_flow_kernel, which this kernel follows
-        // as a programmatic dependent: everything above ran while that kernel did.
-        grid_dependency_wait();
-        const __half *f1 = a.flow1 + n * 2 * static_cast<int64_t>(plane);
-        const __half *f2 = a.flow2 + n * 2 * static_cast<int64_t>(plane);
-        __half *out_prop = cond + ch0 * plane, *out_n2 = cond + (128 + ch0) * plane;
+        // Map 1 reads the second-order flow from second_order_flow_kernel, which this kernel
+        // follows as a programmatic dependent: everything above ran while that kernel did.  Map 0
+        // reads flow1, an input, and writes nothing that kernel writes.
+        if (map) grid_dependency_wait();
+        const __half *fl = map ? a.flow2 + n * 2 * static_cast<int64_t>(plane)
+                               : a.flow1 + n * 2 * static_cast<int64_t>(plane);
+        __half *out = cond + (128 * map + ch0) * plane;
         int y = y_first, x = x_first;
-        // The four flow values of the next pixel are loaded one iteration ahead.
-        __half n1x = __float2half_rn(0.0f), n1y = n1x, n2x = n1x, n2y = n1x;
+        // The two flow values of the next pixel are loaded one iteration ahead.
+        __half nfx = __float2half_rn(0.0f), nfy = nfx;
         if (static_cast<int>(threadIdx.x) < plane) {
-            n1x = f1[threadIdx.x], n1y = f1[plane + threadIdx.x];
-            n2x = f2[threadIdx.x], n2y = f2[plane + threadIdx.x];
+            nfx = fl[threadIdx.x];
+            nfy = fl[plane + threadIdx.x];
         }
 #pragma unroll 2
         for (int p = threadIdx.x; p < plane; p += kTsThreads) {
             const float fy = static_cast<float>(y), fx = static_cast<float>(x);
-            const float f1x = __half2float(n1x), f1y = __half2float(n1y);
-            const float f2x = __half2float(n2x), f2y = __half2float(n2y);
+            const float vx = __half2float(nfx), vy = __half2float(nfy);
             if (p + kTsThreads < plane) {
-                n1x = f1[p + kTsThreads], n1y = f1[plane + p + kTsThreads];
-                n2x = f2[p + kTsThreads], n2y = f2[plane + p + kTsThreads];
+                nfx = fl[p + kTsThreads];
+                nfy = fl[plane + p + kTsThreads];
             }
-            const SlabCorners c1 = slab_corners(__fadd_rn(fy, f1y), __fadd_rn(fx, f1x), H, W);
-            const SlabCorners c2 = slab_corners(__fadd_rn(fy, f2y), __fadd_rn(fx, f2x), H, W);
-#pragma unroll
-            for (int which = 0; which < 2; ++which) {
-                const SlabCorners &c = which ? c2 : c1;
-                const uint2 *s_ = which ? n2_s : prop_s;
-                __half *o = (which ? out_n2 : out_prop) + p;
-                uint2 q00 = make_uint2(0u, 0u), q01 = q00, q10 = q00, q11 = q00;
-                if (c.in) {
-                    q00 = s_[c.idx];
-                    q01 = s_[c.idx + 1];
-                    q10 = s_[c.idx + sw];
-                    q11 = s_[c.idx + sw + 1];
-                }
-                // Each 32-bit word holds two channels: one paired conversion per word.
-                const float2 a00 = pair_to_float2(q00.x), b00 = pair_to_float2(q00.y);
-                const float2 a01 = pair_to_float2(q01.x), b01 = pair_to_float2(q01.y);
-                const float2 a10 = pair_to_float2(q10.x), b10 = pair_to_float2(q10.y);
-                const float2 a11 = pair_to_float2(q11.x), b11 = pair_to_float2(q11.y);
-                o[0] = __float2half_rn(bilinear_terms(a00.x, a01.x, a10.x, a11.x, c.ly, c.lx));
-                o[plane] = __float2half_rn(bilinear_terms(a00.y, a01.y, a10.y, a11.y, c.ly, c.lx));
-                o[2 * plane] = __float2half_rn(bilinear_terms(b00.x, b01.x, b10.x, b11.x, c.ly, c.lx));
-                o[3 * plane] = __float2half_rn(bilinear_terms(b00.y, b01.y, b10.y, b11.y, c.ly, c.lx));
+            const SlabCorners c = slab_corners(__fadd_rn(fy, vy), __fadd_rn(fx, vx), H, W);
+            __half *o = out + p;
+            uint2 q00 = make_uint2(0u, 0u), q01 = q00, q10 = q00, q11 = q00;
+            if (c.in) {
+                q00 = slab_s[c.idx];
+                q01 = slab_s[c.idx + 1];
+                q10 = slab_s[c.idx + sw];
+                q11 = slab_s[c.idx + sw + 1];
             }
+            // Each 32-bit word holds two channels: one paired conversion per word.
+            const float2 a00 = pair_to_float2(q00.x), b00 = pair_to_float2(q00.y);
+            const float2 a01 = pair_to_float2(q01.x), b01 = pair_to_float2(q01.y);
+            const float2 a10 = pair_to_float2(q10.x), b10 = pair_to_float2(q10.y);
+            const float2 a11 = pair_to_float2(q11.x), b11 = pair_to_float2(q11.y);
+            o[0] = __float2half_rn(bilinear_terms(a00.x, a01.x, a10.x, a11.x, c.ly, c.lx));
+            o[plane] = __float2half_rn(bilinear_terms(a00.y, a01.y, a10.y, a11.y, c.ly, c.lx));
+            o[2 * plane] = __float2half_rn(bilinear_terms(b00.x, b01.x, b10.x, b11.x, c.ly, c.lx));
+            o[3 * plane] = __float2half_rn(bilinear_terms(b00.y, b01.y, b10.y, b11.y, c.ly, c.lx));
             y += step_y;
             x += step_x;
             if (x >= W) {
@@ -305,7 +294,7 @@ __global__ void __launch_bounds__(kTsThreads) temporal_prepare_staged_kernel(con
                 ++y;
             }
         }
-        __syncthreads();  // the slabs are rewritten for the next frame
+        __syncthreads();  // the slab is rewritten for the next frame
     }
 }
 
@@ -340,8 +329,9 @@ __global__ void __launch_bounds__(kTsThreads) second_order_flow_kernel(const Tem
 
 }  // namespace
 
-// Shared memory of the staged kernel for a frame (two slabs), or 0 when they exceed 110 KB, which
-// keeps at least two blocks per SM (a 64x64 frame takes 69.7 KB: three).
+// Shared memory of the staged kernel for a frame (one 4-channel slab), or 0 when it exceeds 110 KB,
+// which keeps at least two blocks per SM (a 64x64 frame takes 34.8 KB: five blocks, a register
+// limit).
 size_t temporal_staged_smem(int height, int width) {
     const size_t bytes = static_cast<size_t>(height + 2) * (width + 2) * kTsBytesPerPosition;
     return bytes <= 110 * 1024 ? bytes : 0;
@@ -373,8 +363,9 @@ cudaError_t launch_temporal_prepare(int n, int height, int width, const __half *
                                    stream>>>(a);
         cudaError_t e = cudaGetLastError();
         if (e != cudaSuccess) return e;
-        const int64_t blocks = static_cast<int64_t>(n) * kTsSlices;
-        const unsigned grid = static_cast<unsigned>(blocks < 65535LL * kTsSlices ? blocks : 65535LL * kTsSlices);
+        const int64_t blocks = static_cast<int64_t>(n) * 2 * kTsSlices;
+        const unsigned grid =
+            static_cast<unsigned>(blocks < 65535LL * 2 * kTsSlices ? blocks : 65535LL * 2 * kTsSlices);
         return launch_dependent(temporal_prepare_staged_kernel, dim3(grid), dim3(kTsThreads), smem, stream, a);
     }
     const int64_t plane = static_cast<int64_t>(height) * width;
