@@ -62,11 +62,14 @@ def load_peaks():
 
 
 class ClockSampler:
-    """nvidia-smi samples every 200 ms during the timed region (clocks and throttle reasons)."""
+    """nvidia-smi samples every 50 ms (clocks and throttle reasons, each with nvidia-smi's own
+    timestamp); `stop(window)` keeps the samples taken inside the timed region, or all of them,
+    marked so, when the region is too short to hold one."""
 
-    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+    QUERY = ("timestamp,index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    PERIOD_MS = 50
 
     def __init__(self, gpu_index: int):
         self.gpu = gpu_index
@@ -78,7 +81,7 @@ class ClockSampler:
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
-                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+                 "-lms", str(self.PERIOD_MS)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except OSError:
             self.proc = None
             return
@@ -89,7 +92,32 @@ class ClockSampler:
         for line in self.proc.stdout:
             self.lines.append(line.strip())
 
-    def stop(self) -> dict:
+    @staticmethod
+    def summarize(lines, window=None) -> dict:
+        """Median SM clock, max clock and the slowdown reasons seen, from nvidia-smi CSV lines;
+        `window` = (t0, t1) in seconds since the epoch selects the samples of the timed region."""
+        import datetime
+
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        rows = []
+        for ln in lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 10:
+                continue
+            try:
+                ts = datetime.datetime.strptime(parts[0], "%Y/%m/%d %H:%M:%S.%f").timestamp()
+                rows.append((ts, float(parts[2]), float(parts[3]),
+                             {n for n, v in zip(names, parts[6:10]) if v.lower() == "active"}))
+            except ValueError:
+                continue
+        inside = [r for r in rows if window is not None and window[0] <= r[0] <= window[1]]
+        use = inside or rows
+        reasons = set().union(*[r[3] for r in use]) if use else set()
+        return {"sm_mhz": statistics.median(r[1] for r in use) if use else None,
+                "sm_max_mhz": use[-1][2] if use else None, "reasons": sorted(reasons), "samples": len(use),
+                "samples_in_timed_region": len(inside), "period_ms": ClockSampler.PERIOD_MS}
+
+    def stop(self, window=None) -> dict:
         if self.proc is not None:
             self.proc.terminate()
             try:
@@ -98,22 +126,7 @@ class ClockSampler:
                 self.proc.kill()
             if self._thread is not None:
                 self._thread.join(timeout=2)
-        sm, mx, reasons = [], None, set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in self.lines:
-            parts = [p.strip() for p in ln.split(",")]
-            if len(parts) < 9:
-                continue
-            try:
-                sm.append(float(parts[1]))
-                mx = float(parts[2])
-            except ValueError:
-                continue
-            for name, val in zip(names, parts[5:9]):
-                if val.lower() == "active":
-                    reasons.add(name)
-        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
-                "samples": len(sm)}
+        return self.summarize(self.lines, window)
 
 
 # ----------------------------------------------------------------------------- distributed
@@ -501,10 +514,13 @@ def run_ours(args):
     time.sleep(0.3)
     barrier(pg)
     torch.cuda.synchronize(dev)
+    t_begin = time.time()
     ms = event_time_ms(step, args.steps)
     torch.cuda.synchronize(dev)
+    t_end = time.time()
     barrier(pg)
-    clocks = sampler.stop()
+    time.sleep(0.1)  # let the sampler's last in-region line arrive
+    clocks = sampler.stop(window=(t_begin, t_end))
     ms_max = max_over_ranks(ms, pg)
     ms_per_step = ms_max / args.steps
     value = job_px / (ms_per_step * 1e-3) / 1e6  # whole job, Mpx/s
