@@ -332,6 +332,82 @@ static void check_errors(void) {
     cudaFree(buf);
 }
 
+/* FP16 bits of a float, rounded to nearest even. */
+static uint16_t half_bits_rne(float v) {
+    _Float16 h = (_Float16)v;
+    uint16_t b;
+    memcpy(&b, &h, sizeof b);
+    return b;
+}
+
+/* dcn_temporal_prepare_f16 (runTemporalPreparation's two kernels) on `frames` frames of w x h with
+ * seeded FP16 features and flows, against dcn_oracle_temporal_prepare frame by frame, bit for bit. */
+static void check_temporal(int frames, int w, int h, uint64_t seed) {
+    const int64_t plane = (int64_t)w * h;
+    const int64_t nf = frames * 64 * plane, nflow = frames * 2 * plane;
+    float *in[5];
+    uint16_t *bits[5];
+    const int64_t counts[5] = {nf, nf, nf, nflow, nflow};
+    uint64_t st = seed;
+    for (int t = 0; t < 5; ++t) {
+        in[t] = (float *)malloc(sizeof(float) * (size_t)counts[t]);
+        bits[t] = (uint16_t *)malloc(sizeof(uint16_t) * (size_t)counts[t]);
+        for (int64_t i = 0; i < counts[t]; ++i) {
+            /* features in [-2, 2), flows in [-12, 12) px, 1/256 steps, then FP16 */
+            const float v = t < 3 ? (float)draw(&st, -512, 512) / 256.0f : (float)draw(&st, -3072, 3072) / 256.0f;
+            bits[t][i] = half_bits_rne(v);
+            in[t][i] = half_to_float(bits[t][i]);
+        }
+    }
+    void *d_in[5], *d_cond, *d_di, *d_flow2;
+    for (int t = 0; t < 5; ++t) {
+        CUDA_OK(cudaMalloc(&d_in[t], sizeof(uint16_t) * (size_t)counts[t]));
+        CUDA_OK(cudaMemcpy(d_in[t], bits[t], sizeof(uint16_t) * (size_t)counts[t], cudaMemcpyHostToDevice));
+    }
+    const int64_t ncond = frames * 196 * plane, ndi = frames * 128 * plane;
+    CUDA_OK(cudaMalloc(&d_cond, sizeof(uint16_t) * (size_t)ncond));
+    CUDA_OK(cudaMalloc(&d_di, sizeof(uint16_t) * (size_t)ndi));
+    CUDA_OK(cudaMalloc(&d_flow2, sizeof(uint16_t) * (size_t)nflow));
+    const dcn_status rc = dcn_temporal_prepare_f16(frames, w, h, d_in[0], d_in[1], d_in[2], d_in[3], d_in[4], 1,
+                                                   d_cond, d_di, d_flow2, NULL);
+    CHECK(rc == DCN_OK, "temporal %dx%d: %s", w, h, dcn_status_string(rc));
+    CUDA_OK(cudaDeviceSynchronize());
+    uint16_t *cond = (uint16_t *)malloc(sizeof(uint16_t) * (size_t)ncond);
+    uint16_t *di = (uint16_t *)malloc(sizeof(uint16_t) * (size_t)ndi);
+    uint16_t *flow2 = (uint16_t *)malloc(sizeof(uint16_t) * (size_t)nflow);
+    CUDA_OK(cudaMemcpy(cond, d_cond, sizeof(uint16_t) * (size_t)ncond, cudaMemcpyDeviceToHost));
+    CUDA_OK(cudaMemcpy(di, d_di, sizeof(uint16_t) * (size_t)ndi, cudaMemcpyDeviceToHost));
+    CUDA_OK(cudaMemcpy(flow2, d_flow2, sizeof(uint16_t) * (size_t)nflow, cudaMemcpyDeviceToHost));
+    float *rc_cond = (float *)malloc(sizeof(float) * (size_t)(196 * plane));
+    float *rc_di = (float *)malloc(sizeof(float) * (size_t)(128 * plane));
+    float *rc_flow2 = (float *)malloc(sizeof(float) * (size_t)(2 * plane));
+    int64_t mismatches = 0;
+    for (int f = 0; f < frames; ++f) {
+        dcn_oracle_temporal_prepare(w, h, in[0] + f * 64 * plane, in[1] + f * 64 * plane, in[2] + f * 64 * plane,
+                                    in[3] + f * 2 * plane, in[4] + f * 2 * plane, 1, rc_cond, rc_di, rc_flow2);
+        for (int64_t i = 0; i < 196 * plane; ++i) mismatches += cond[f * 196 * plane + i] != half_bits_rne(rc_cond[i]);
+        for (int64_t i = 0; i < 128 * plane; ++i) mismatches += di[f * 128 * plane + i] != half_bits_rne(rc_di[i]);
+        for (int64_t i = 0; i < 2 * plane; ++i) mismatches += flow2[f * 2 * plane + i] != half_bits_rne(rc_flow2[i]);
+    }
+    CHECK(mismatches == 0, "temporal %dx%d x%d: %lld values differ from the oracle", w, h, frames,
+          (long long)mismatches);
+    printf("temporal preparation %dx%d x%d: bit-exact against the oracle\n", w, h, frames);
+    for (int t = 0; t < 5; ++t) {
+        free(in[t]);
+        free(bits[t]);
+        cudaFree(d_in[t]);
+    }
+    cudaFree(d_cond);
+    cudaFree(d_di);
+    cudaFree(d_flow2);
+    free(cond);
+    free(di);
+    free(flow2);
+    free(rc_cond);
+    free(rc_di);
+    free(rc_flow2);
+}
+
 int main(void) {
     int dev_count = 0;
     if (cudaGetDeviceCount(&dev_count) != cudaSuccess || dev_count == 0) {
@@ -346,6 +422,8 @@ int main(void) {
     const dcn_shape five = jasna_shape(5, 16, 24);
     check_f16_host(&five, 14, 2);
     check_f32(&slab, 13);
+    check_temporal(2, 64, 64, 15);  /* the shared-memory form */
+    check_temporal(1, 17, 13, 16);  /* an odd pixel count: the global-memory form */
     check_errors();
     if (failures) {
         printf("FAILED (%d)\n", failures);

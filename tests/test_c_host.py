@@ -2,7 +2,8 @@
 C-ABI caller would write, with device memory from the CUDA runtime and no Python or torch in
 the process.  Without a GPU it must compile and link against include/dcn_b200.h and the built
 library (the header is plain C); on a B200 it runs the FP16 operator on both tensor-core paths,
-the bit-exact FP32 path, the non-finite flag and the error codes against the C oracle."""
+the bit-exact FP32 path, the temporal preparation (both its forms, bit-exact), the non-finite flag
+and the error codes against the C oracle."""
 
 from __future__ import annotations
 
