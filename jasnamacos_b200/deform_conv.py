@@ -130,6 +130,19 @@ class TemporalPreparationResult:
 
 
 @dataclass(frozen=True)
+class TemporalPreparationProbeResult:
+    """TemporalPreparationProbeResult (TemporalPreparationProbe.swift:3-12)."""
+    median_milliseconds: float
+    minimum_milliseconds: float
+    maximum_milliseconds: float
+    iterations: int
+    maximum_magnitude: float
+    repeat_maximum_error: float
+    first_order_zero_maximum_error: float
+    checksum: float
+
+
+@dataclass(frozen=True)
 class DeformConvShape:
     """`struct DeformConvShape` (DeformConv.swift:3-42), same fields in the same order."""
 
@@ -616,6 +629,71 @@ class CudaDeformConv:
         self.device_error()
         return TemporalPreparationResult(float(start.elapsed_time(end)), cond.cpu().numpy(), di.cpu().numpy(),
                                          flow2.cpu().numpy())
+
+    def verify_temporal_preparation(self, backward_flow, forward_flow) -> TemporalPreparationProbeResult:
+        """`verifyTemporalPreparation(runner:backwardFlow:forwardFlow:)`
+        (TemporalPreparationProbe.swift:14-101): 64x64 frames built with the probe's feature
+        formula, each direction's flow used as both flow1 and the previous flow; two warm-up
+        passes, then eight timed passes (backward + forward, GPU time each), then one first-order
+        pass with zero feat_n2.  Raises CommandFailed, as the probe throws, unless the conditions
+        are finite and not all tiny, the timed passes repeat within 0.001 and the first-order
+        second-order flow is exactly zero."""
+        torch = _torch()
+        w = h = 64
+        plane = w * h
+        arrays = [np.ascontiguousarray(a, dtype=np.float16).reshape(-1) for a in (backward_flow, forward_flow)]
+        if any(a.size != 2 * plane for a in arrays):
+            raise InvalidShape()
+
+        def features(seed):
+            i = np.arange(64 * plane, dtype=np.int64)
+            return ((((i * 37 + seed) % 509).astype(np.float32) / np.float32(508) - np.float32(0.5))
+                    * np.float32(0.5)).astype(np.float16)
+
+        dev = self.device
+        up = lambda a: torch.from_numpy(a).to(dev)  # noqa: E731
+        feat_prop, feat_current, feat_n2 = up(features(17)), up(features(31)), up(features(47))
+        zero = torch.zeros(64 * plane, dtype=torch.float16, device=dev)
+        flows = [up(a) for a in arrays]
+
+        def execute(second_order):
+            outs, ms = [], 0.0
+            for flow in flows:
+                start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                start.record()
+                res = self.temporal_prepare(w, h, feat_prop, feat_current, feat_n2 if second_order else zero,
+                                            flow, flow, second_order)
+                end.record()
+                end.synchronize()
+                ms += float(start.elapsed_time(end))
+                outs.append(res)
+            self.device_error()
+            return ms, outs
+
+        execute(True)
+        execute(True)
+        first_ms, first = execute(True)
+        samples, last = [first_ms], first
+        for _ in range(1, 8):
+            ms, last = execute(True)
+            samples.append(ms)
+        _, first_order = execute(False)
+        samples.sort()
+        max_mag = rep = zero_err = 0.0
+        checksum = 0.0
+        for d in range(2):
+            cur = last[d][0].float().cpu().numpy()
+            if not np.isfinite(cur).all():
+                raise CommandFailed("temporal preparation produced a non-finite condition")
+            max_mag = max(max_mag, float(np.abs(cur).max()))
+            rep = max(rep, float(np.abs(first[d][0].float().cpu().numpy() - cur).max()))
+            checksum += float(cur[::4099].astype(np.float64).sum())
+            zero_err = max(zero_err, float(first_order[d][2].float().abs().max().item()))
+        if not (max_mag > 0.001 and rep <= 0.001 and zero_err == 0.0):
+            raise CommandFailed(f"temporal preparation validation failed (max={max_mag}, repeat={rep}, "
+                                f"zero={zero_err})")
+        return TemporalPreparationProbeResult(samples[len(samples) // 2], samples[0], samples[-1], len(samples),
+                                              max_mag, rep, zero_err, checksum)
 
     # -- benchmark (benchmarkJasnaShape) ----------------------------------------
     def benchmark_jasna_shape(self, iterations: int = 20, weight_set=None, seed: int = 0x4A41534E41):

@@ -178,3 +178,24 @@ def test_irregular_frames_bit_exact(cuda_op, w, h):
         want = oracle.temporal_prepare(w, h, sl(prop, 64), sl(cur, 64), sl(n2, 64), sl(f1, 2), sl(prev, 2), True)
         for a, b, c in zip(got, want, (196, 128, 2)):
             assert np.array_equal(sl(a, c), b), (w, h, f, c)
+
+
+def test_verify_temporal_preparation_probe(cuda_op):
+    """verify_temporal_preparation mirrors the reference's probe (TemporalPreparationProbe.swift:
+    14-101): eight timed bidirectional passes that repeat exactly, conditions that are not all tiny,
+    and an exactly zero second-order flow on the first-order pass; a flow with a NaN makes the
+    conditions non-finite, which the probe reports as a failed command.  (A NaN position floors
+    to 0, inside the frame, so no load leaves its buffer.)"""
+    from jasnamacos_b200.deform_conv import CommandFailed
+
+    plane = 64 * 64
+    backward, forward = _flows(plane, 4.0, 7), _flows(plane, 4.0, 8)
+    res = cuda_op.verify_temporal_preparation(backward, forward)
+    assert res.iterations == 8
+    assert res.repeat_maximum_error == 0.0 and res.first_order_zero_maximum_error == 0.0
+    assert res.maximum_magnitude > 0.001 and np.isfinite(res.checksum)
+    assert 0.0 < res.minimum_milliseconds <= res.median_milliseconds <= res.maximum_milliseconds
+    bad = backward.copy()
+    bad[123] = np.nan
+    with pytest.raises(CommandFailed):
+        cuda_op.verify_temporal_preparation(bad, forward)
