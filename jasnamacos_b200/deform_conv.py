@@ -607,6 +607,22 @@ class CudaDeformConv:
             raise NonFiniteOutput("Inf/NaN in the DCNv2 output")
         return out.cpu().numpy()
 
+    def run_dcn_offset_transform(self, plane: int, raw, flow1, flow2) -> tuple[np.ndarray, np.ndarray]:
+        """`runDCNOffsetTransform(plane:raw:flow1:flow2:)` (MetalRunner.swift:469-508): the offset
+        network's raw output (432 channels of `plane` pixels) and the two flows (2 channels each) as
+        FP16 host arrays in; the DCN offsets (288 channels, 10*tanh(raw) plus the flow, y first)
+        and the mask (144 channels, sigmoid(raw)) out as FP16 host arrays.  Sizes that do not match
+        `plane` raise InvalidShape, as the reference throws invalidShape."""
+        torch = _torch()
+        arrays = [np.ascontiguousarray(a, dtype=np.float16).reshape(-1) for a in (raw, flow1, flow2)]
+        if plane <= 0 or [a.size for a in arrays] != [432 * plane, 2 * plane, 2 * plane]:
+            raise InvalidShape()
+        dev = self.device
+        offset, mask = self.prepare_offsets(plane, *(torch.from_numpy(a).to(dev) for a in arrays))
+        torch.cuda.synchronize(dev)
+        self.device_error()
+        return offset.cpu().numpy(), mask.cpu().numpy()
+
     def run_temporal_preparation(self, width: int, height: int, feat_prop, feat_current, feat_n2, flow1,
                                  previous_flow, has_second_order: bool) -> "TemporalPreparationResult":
         """`runTemporalPreparation(width:height:featProp:featCurrent:featN2:flow1:previousFlow:

@@ -64,6 +64,44 @@ def test_offset_transform_reference_cli_case(cuda_op):
     assert err < kat["tolerance"]  # JasnaCLI.swift:208
 
 
+def test_run_dcn_offset_transform_host_arrays(cuda_op):
+    """runDCNOffsetTransform's host-array form (MetalRunner.swift:469-508): the reference CLI's
+    plane-7 case under its 0.005 gate (JasnaCLI.swift:177-211), the same bits as the device-tensor
+    entry, and a 4096-pixel plane with raw values that saturate tanh and the sigmoid; sizes that do
+    not match the plane raise InvalidShape."""
+    import torch
+
+    from jasnamacos_b200.deform_conv import InvalidShape
+
+    kat = reference_kats()["offset_transform"]
+    plane = kat["plane"]
+    raw, f1, f2 = (np.array(kat[k], np.float32) for k in ("raw", "flow1", "flow2"))
+    off, msk = cuda_op.run_dcn_offset_transform(plane, raw, f1, f2)
+    assert off.dtype == np.float16 and off.shape == (288 * plane,) and msk.shape == (144 * plane,)
+    ref_off, ref_msk = oracle.prepare_offsets(plane, raw, f1, f2)
+    err = max(np.abs(off.astype(np.float32) - ref_off).max(), np.abs(msk.astype(np.float32) - ref_msk).max())
+    assert err < kat["tolerance"]
+    d_off, d_msk = cuda_op.prepare_offsets(plane, *(torch.from_numpy(a).half().cuda() for a in (raw, f1, f2)))
+    torch.cuda.synchronize()
+    assert np.array_equal(off, d_off.cpu().numpy()) and np.array_equal(msk, d_msk.cpu().numpy())
+
+    plane = 64 * 64
+    g = np.random.default_rng(21)
+    f16 = lambda a: a.astype(np.float16).astype(np.float32)  # noqa: E731
+    raw, f1, f2 = f16(g.uniform(-12, 12, 432 * plane)), f16(g.uniform(-16, 16, 2 * plane)), f16(
+        g.uniform(-16, 16, 2 * plane))
+    off, msk = cuda_op.run_dcn_offset_transform(plane, raw, f1, f2)
+    ref_off, ref_msk = oracle.prepare_offsets(plane, raw, f1, f2)
+    # one FP16 rounding of offsets below 26 in magnitude (ulp 2^-6 there) and of masks in [0, 1]
+    assert np.abs(off.astype(np.float32) - ref_off).max() <= 2.0 ** -6
+    assert np.abs(msk.astype(np.float32) - ref_msk).max() <= 2.0 ** -11
+    assert np.isfinite(off.astype(np.float32)).all() and msk.min() >= 0 and msk.max() <= 1
+    with pytest.raises(InvalidShape):
+        cuda_op.run_dcn_offset_transform(plane, raw[:-1], f1, f2)
+    with pytest.raises(InvalidShape):
+        cuda_op.run_dcn_offset_transform(0, raw[:0], f1[:0], f2[:0])
+
+
 def test_misaligned_pointers_are_rejected_on_the_host(cuda_op):
     import torch
 
