@@ -366,10 +366,14 @@ TEMPORAL_BYTES_PER_PX = 2 * (3 * 64 + 2 + 2) + 2 * (196 + 2)
 TEMPORAL_DEFORM_INPUT_BYTES_PER_PX = 2 * 128
 
 
-def temporal_section(op, dev, frames: int, steps: int, peaks: dict) -> dict:
+def temporal_section(op, dev, frames: int, steps: int, peaks: dict, dcn=None) -> dict:
     """The temporal preparation in front of the DCN (dcn_temporal_prepare_f16) on `frames` 64x64
     frames -- the benchmark's tile count -- with and without the deform-input copy: device time
-    (CUDA events), HBM roofline, and the first and last frames against the oracle (bit-exact)."""
+    (CUDA events), HBM roofline, and the first and last frames against the oracle (bit-exact).
+    With `dcn` = (packed weight, bias), also the alignment step it feeds: temporal preparation +
+    the raw-form DCN, once with the NCHW deform input (the DCN regroups it) and once with the
+    deform input written in the DCN's slab layout (dcn_temporal_prepare_slabs_f16 +
+    dcn_forward_f16_raw_grouped, no pre-pass); the two outputs must be bit-identical."""
     import numpy as np
     import torch
 
@@ -426,6 +430,8 @@ def temporal_section(op, dev, frames: int, steps: int, peaks: dict) -> dict:
             "what": "two single-frame calls (backward and forward directions, deform input included) per step, "
                     "as the reference's temporal probe times them; CUDA-graph replays. The reference publishes "
                     "0.284-0.289 ms median for this on an M4 GPU (Metal, not measurable here)"}
+    if dcn is not None:
+        out["chain"] = chain_section(op, dev, w, h, frames, steps, feats, flows, cond, di, flow2, *dcn)
     run(True)()
     torch.cuda.synchronize(dev)
     mismatches, compared = 0, 0
@@ -443,6 +449,53 @@ def temporal_section(op, dev, frames: int, steps: int, peaks: dict) -> dict:
                      "passed": mismatches == 0}
     del feats, flows, cond, di, flow2
     return out
+
+
+def chain_section(op, dev, w, h, frames, steps, feats, flows, cond, di, flow2, packed, bias) -> dict:
+    """Temporal preparation + raw-form DCN (the offset network between them is not part of this
+    path; a seeded raw tensor stands in for its output), timed both ways on one stream."""
+    import torch
+
+    from jasnamacos_b200.deform_conv import DeformConvShape
+
+    plane = w * h
+    shape = DeformConvShape.jasna_propagation(frames, h, w)
+    g = torch.Generator(device=dev).manual_seed(977)
+    raw = torch.randn(frames * 432 * plane, generator=g, device=dev, dtype=torch.float16)
+    dcn_out = torch.empty(shape.output_count, dtype=torch.float16, device=dev)
+    flag = torch.zeros(1, dtype=torch.int32, device=dev)
+    ws = torch.empty(max(op.raw_workspace_bytes(shape), op.temporal_slabs_bytes(w, h, frames)), dtype=torch.uint8,
+                     device=dev)
+
+    def nchw():
+        op.temporal_prepare(w, h, *feats, *flows, True, batch=frames, conditions=cond, deform_input=di, flow2=flow2)
+        op.forward_f16_raw(shape, di, raw, flows[0], flow2, packed, bias, out=dcn_out, flag=flag, workspace=ws)
+
+    def slabs():
+        op.temporal_prepare_slabs(w, h, *feats, *flows, True, batch=frames, workspace=ws, conditions=cond,
+                                  flow2=flow2)
+        op.forward_f16_raw_grouped(shape, ws, raw, flows[0], flow2, packed, bias, out=dcn_out, flag=flag)
+
+    res = {"what": "temporal preparation + dcn_forward_f16_raw on the NCHW deform input (regroup pre-pass "
+                   "inside), against dcn_temporal_prepare_slabs_f16 + dcn_forward_f16_raw_grouped (deform "
+                   "input written in the DCN's slab layout, no pre-pass)"}
+    outs = {}
+    for name, fn in (("nchw", nchw), ("slabs", slabs)):
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize(dev)
+        outs[name] = dcn_out.clone()
+        ms = event_time_ms(fn, steps) / steps
+        res[name] = {"ms": ms, "Mpx_s": frames * plane / (ms * 1e-3) / 1e6}
+    prep = lambda: op.temporal_prepare_slabs(w, h, *feats, *flows, True, batch=frames, workspace=ws,  # noqa: E731
+                                             conditions=cond, flow2=flow2)
+    res["slabs"]["temporal_prepare_slabs_ms"] = event_time_ms(prep, steps) / steps
+    torch.cuda.synchronize(dev)
+    res["saved_ms"] = res["nchw"]["ms"] - res["slabs"]["ms"]
+    res["outputs_bit_identical"] = bool(torch.equal(outs["nchw"], outs["slabs"]))
+    res["nonfinite_flag"] = int(flag.item())
+    del raw, dcn_out, ws, outs
+    return res
 
 
 # Benchmark configurations.  Tile batches (2, 4) are sharded over the GPUs (total work
@@ -582,7 +635,7 @@ def run_ours(args):
     # ---- temporal preparation in front of the DCN (config 4, one GPU) ---------------------
     temporal = None
     if args.config == 4 and world == 1 and not args.no_temporal:
-        temporal = temporal_section(op, dev, i_end - i_begin, args.steps, peaks)
+        temporal = temporal_section(op, dev, i_end - i_begin, args.steps, peaks, dcn=(packed, b16))
         torch.cuda.empty_cache()
 
     # ---- final gather of every shard's output to rank 0 (N > 1) -------------------------

@@ -288,6 +288,16 @@ dcn_status dcn_forward_f16_raw(const dcn_shape *shape, const void *input, const 
                                const void *flow1, const void *flow2, const void *packed_weight,
                                const void *bias, void *output, uint32_t *nonfinite_flag,
                                void *workspace, size_t workspace_bytes, dcn_stream stream);
+/* The raw form on an input already in its path's grouped layout at the start of
+ * `workspace` (written by dcn_regroup_input_f16 or by dcn_temporal_prepare_slabs_f16):
+ * dcn_forward_f16_raw without its pre-pass, as dcn_forward_f16_grouped is dcn_forward_f16
+ * without it.  workspace 16-byte aligned, workspace_bytes at least
+ * dcn_forward_f16_raw_workspace_bytes(shape); the grouped input is read, not changed. */
+dcn_status dcn_forward_f16_raw_grouped(const dcn_shape *shape, void *workspace, const void *raw,
+                                       const void *flow1, const void *flow2,
+                                       const void *packed_weight, const void *bias, void *output,
+                                       uint32_t *nonfinite_flag, size_t workspace_bytes,
+                                       dcn_stream stream);
 
 /* ---- tensor plumbing: split input, output slot --------------------------------
  * Where the FP16 operator reads its input channels and writes its output channels,
@@ -359,6 +369,28 @@ dcn_status dcn_temporal_prepare_f16(int32_t batch, int32_t width, int32_t height
                                     const void *feat_current, const void *feat_n2, const void *flow1,
                                     const void *previous_flow, int32_t has_second_order, void *conditions,
                                     void *deform_input, void *flow2, dcn_stream stream);
+
+/* The same preparation with the deform input [feat_prop, feat_n2] written in the layout the
+ * DCN's slab kernel reads (dcn_regroup_input_f16's DCN_PATH_SLAB_TC layout for the
+ * 128-channel, 16-group Jasna shape: slabs [batch][16][H+2][W+2][8] FP16, zero ring
+ * included) at the start of `workspace`, instead of as an NCHW tensor.  This is where
+ * assemble_temporal_alignment_fp16 writes the DCN's input in the reference
+ * (MetalShader.swift:769-813); writing it here in the DCN's own layout lets the DCN skip its
+ * regroup pre-pass: pass the same workspace to dcn_forward_f16_grouped or
+ * dcn_forward_f16_raw_grouped.  The bytes equal what dcn_regroup_input_f16 makes of the
+ * NCHW deform input.  dcn_temporal_slabs_bytes gives the slab bytes (0 for frames this form
+ * does not take: the form needs the shared-memory kernel, (H+2)(W+2) <= 14,080, which covers
+ * every frame the slab kernel takes); it returns DCN_ERR_UNSUPPORTED for those and for an odd
+ * pixel count.  feat_prop, feat_current, feat_n2, conditions and workspace 16-byte aligned;
+ * workspace_bytes at least dcn_temporal_slabs_bytes (the DCN entry points want their own
+ * workspace size, which is at least that). */
+size_t dcn_temporal_slabs_bytes(int32_t batch, int32_t width, int32_t height);
+dcn_status dcn_temporal_prepare_slabs_f16(int32_t batch, int32_t width, int32_t height,
+                                          const void *feat_prop, const void *feat_current,
+                                          const void *feat_n2, const void *flow1,
+                                          const void *previous_flow, int32_t has_second_order,
+                                          void *conditions, void *flow2, void *workspace,
+                                          size_t workspace_bytes, dcn_stream stream);
 
 /* ---- fused FP16 path without any caller allocation ----------------------------
  * No counterpart in the reference.  For callers that cannot allocate device

@@ -127,6 +127,10 @@ PROTOTYPES = {
         ctypes.c_int,
         [_SHAPE, _P, _P, _P, _P, _P, _P, _P, _P, _P, ctypes.c_size_t, _P],
     ),
+    "dcn_forward_f16_raw_grouped": (
+        ctypes.c_int,
+        [_SHAPE, _P, _P, _P, _P, _P, _P, _P, _P, ctypes.c_size_t, _P],
+    ),
     "dcn_forward_f16_io": (
         ctypes.c_int,
         [_SHAPE, _IO, _P, _P, _P, _P, _P, _P, _P, _P, ctypes.c_size_t, _P],
@@ -139,6 +143,9 @@ PROTOTYPES = {
     "dcn_prepare_offsets_f16": (ctypes.c_int, [ctypes.c_int64, _P, _P, _P, _P, _P, _P]),
     "dcn_temporal_prepare_f16": (ctypes.c_int, [ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, _P, _P, _P, _P, _P,
                                                 ctypes.c_int32, _P, _P, _P, _P]),
+    "dcn_temporal_slabs_bytes": (ctypes.c_size_t, [ctypes.c_int32, ctypes.c_int32, ctypes.c_int32]),
+    "dcn_temporal_prepare_slabs_f16": (ctypes.c_int, [ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, _P, _P, _P, _P,
+                                                      _P, ctypes.c_int32, _P, _P, _P, ctypes.c_size_t, _P]),
     "dcn_device_error": (ctypes.c_int, []),
     "dcn_check_wait_timeout": (ctypes.c_int, [ctypes.c_uint32, _P]),
     "dcn_forward_f16_host_workspace_bytes": (ctypes.c_size_t, [_SHAPE, ctypes.c_int32]),

@@ -68,7 +68,8 @@ cudaError_t launch_slab_grouped(const Params &p, const void *slabs, const __half
 cudaError_t launch_temporal_prepare(int n, int height, int width, const __half *feat_prop, const __half *feat_current,
                                     const __half *feat_n2, const __half *flow1, const __half *previous,
                                     bool has_second_order, __half *conditions, __half *deform_input, __half *flow2,
-                                    cudaStream_t stream);
+                                    void *slabs, cudaStream_t stream);
+size_t temporal_staged_smem(int height, int width);
 
 uint64_t current_context_id() {
     static PFN_cuCtxGetCurrent_v4000 get_current = nullptr;
@@ -538,7 +539,44 @@ dcn_status dcn_temporal_prepare_f16(int32_t batch, int32_t width, int32_t height
         batch, height, width, static_cast<const __half *>(feat_prop), static_cast<const __half *>(feat_current),
         static_cast<const __half *>(feat_n2), static_cast<const __half *>(flow1),
         static_cast<const __half *>(previous_flow), has_second_order != 0, static_cast<__half *>(conditions),
-        static_cast<__half *>(deform_input), static_cast<__half *>(flow2), reinterpret_cast<cudaStream_t>(stream)));
+        static_cast<__half *>(deform_input), static_cast<__half *>(flow2), nullptr,
+        reinterpret_cast<cudaStream_t>(stream)));
+}
+
+size_t dcn_temporal_slabs_bytes(int32_t batch, int32_t width, int32_t height) {
+    if (batch <= 0 || width <= 0 || height <= 0 || temporal_staged_smem(height, width) == 0) return 0;
+    return static_cast<size_t>(batch) * 16 * (height + 2) * (width + 2) * 16;
+}
+
+dcn_status dcn_temporal_prepare_slabs_f16(int32_t batch, int32_t width, int32_t height, const void *feat_prop,
+                                          const void *feat_current, const void *feat_n2, const void *flow1,
+                                          const void *previous_flow, int32_t has_second_order, void *conditions,
+                                          void *flow2, void *workspace, size_t workspace_bytes,
+                                          dcn_stream stream) {
+    if (batch <= 0 || width <= 0 || height <= 0 ||
+        static_cast<int64_t>(width) * height > (int64_t{1} << 31) / 256)
+        return DCN_ERR_INVALID_SHAPE;
+    // The slab form is written by the shared-memory kernel only: frames whose 4-channel slab fits
+    // its 110 KB, with an even pixel count (16-byte plane copies).
+    if (dcn_temporal_slabs_bytes(batch, width, height) == 0 || (static_cast<int64_t>(width) * height) % 2 != 0)
+        return DCN_ERR_UNSUPPORTED;
+    const void *planes[] = {feat_prop, feat_current, feat_n2, conditions};
+    for (const void *q : planes)
+        if (q == nullptr || !aligned(q, 16)) return DCN_ERR_INVALID_ARGUMENT;
+    const void *flows[] = {flow1, previous_flow, flow2};
+    for (const void *q : flows)
+        if (q == nullptr || !aligned(q, 2)) return DCN_ERR_INVALID_ARGUMENT;
+    if (workspace == nullptr || !aligned(workspace, 16) ||
+        workspace_bytes < dcn_temporal_slabs_bytes(batch, width, height))
+        return DCN_ERR_INVALID_ARGUMENT;
+    DeviceInfo *dev = nullptr;
+    dcn_status st = current_device(&dev);
+    if (st != DCN_OK) return st;
+    return from_cuda(launch_temporal_prepare(
+        batch, height, width, static_cast<const __half *>(feat_prop), static_cast<const __half *>(feat_current),
+        static_cast<const __half *>(feat_n2), static_cast<const __half *>(flow1),
+        static_cast<const __half *>(previous_flow), has_second_order != 0, static_cast<__half *>(conditions),
+        nullptr, static_cast<__half *>(flow2), workspace, reinterpret_cast<cudaStream_t>(stream)));
 }
 
 dcn_status dcn_prepare_offsets_f16(int64_t plane, const void *raw, const void *flow1, const void *flow2,
@@ -593,6 +631,36 @@ dcn_status dcn_forward_f16_raw_io(const dcn_shape *shape, const dcn_io *io, cons
     const auto *f2 = static_cast<const __half *>(flow2);
     cudaError_t e = launch_regroup(path, p, in, workspace, s);
     if (e != cudaSuccess) return from_cuda(e);
+    const auto *w = static_cast<const uint8_t *>(packed_weight);
+    const auto *b = static_cast<const __half *>(bias);
+    auto *out = static_cast<__half *>(output);
+    if (path == DCN_PATH_SLAB_TC)
+        return from_cuda(launch_slab_grouped_raw(p, workspace, r, f1, f2, w, b, out, nonfinite_flag, dev->sm_count,
+                                                 dev->err_word, s));
+    return from_cuda(launch_fused_grouped_raw(p, workspace, r, f1, f2, w, b, out, nonfinite_flag, dev->sm_count,
+                                              dev->err_word, s));
+}
+
+dcn_status dcn_forward_f16_raw_grouped(const dcn_shape *shape, void *workspace, const void *raw, const void *flow1,
+                                       const void *flow2, const void *packed_weight, const void *bias, void *output,
+                                       uint32_t *nonfinite_flag, size_t workspace_bytes, dcn_stream stream) {
+    dcn_status st = validate(shape);
+    if (st != DCN_OK) return st;
+    const Params p = make_params(*shape);
+    const dcn_path path = select_path(p);
+    if (path == DCN_PATH_DIRECT || p.OG % 2 != 0) return DCN_ERR_UNSUPPORTED;
+    if (!raw || !flow1 || !flow2 || !packed_weight || !bias || !output) return DCN_ERR_INVALID_ARGUMENT;
+    if (!aligned(raw, 16) || !aligned(flow1, 16) || !aligned(flow2, 16) || !aligned(packed_weight, 16) ||
+        !aligned(bias, 2) || !aligned(output, 2) || (nonfinite_flag && !aligned(nonfinite_flag, 4)))
+        return DCN_ERR_INVALID_ARGUMENT;
+    if (!workspace || !aligned(workspace, 16) || workspace_bytes < dcn_forward_f16_raw_workspace_bytes(shape))
+        return DCN_ERR_INVALID_ARGUMENT;
+    DeviceInfo *dev = nullptr;
+    if ((st = current_device(&dev)) != DCN_OK) return st;
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    const auto *r = static_cast<const __half *>(raw);
+    const auto *f1 = static_cast<const __half *>(flow1);
+    const auto *f2 = static_cast<const __half *>(flow2);
     const auto *w = static_cast<const uint8_t *>(packed_weight);
     const auto *b = static_cast<const __half *>(bias);
     auto *out = static_cast<__half *>(output);

@@ -38,6 +38,7 @@ struct TemporalArgs {
     __half *conditions;                                 // [N][196][H][W]
     __half *deform_input;                               // [N][128][H][W] or null
     __half *flow2;                                      // [N][2][H][W]
+    uint2 *slabs;  // the deform input as the DCN's slabs [N][16][H+2][W+2][8] (16 B per position), or null
     int N, H, W;
     int has_second_order;
 };
@@ -182,6 +183,10 @@ __device__ __forceinline__ float2 pair_to_float2(uint32_t word) {
     return __half22float2(h);
 }
 
+// kSlabs: the deform input is written in the DCN's slab layout (zero ring included) straight from
+// the staging registers, in place of the NCHW copy: each block writes the 8-byte half of every
+// 16-byte position that its 4 channels make in deformable group 8 * map + ch0 / 8.
+template <bool kSlabs>
 __global__ void __launch_bounds__(kTsThreads) temporal_prepare_staged_kernel(const TemporalArgs a) {
     extern __shared__ __align__(16) uint8_t ts_smem[];
     // In-frame offsets are 32-bit (a staged frame holds at most a few thousand pixels); rows and
@@ -213,12 +218,15 @@ __global__ void __launch_bounds__(kTsThreads) temporal_prepare_staged_kernel(con
                 uint4 *cond4 = reinterpret_cast<uint4 *>(cond + (64 + ch0) * plane);
                 for (int i = threadIdx.x; i < vec; i += kTsThreads) cond4[i] = cur4[i];
             }
-            if (di != nullptr) {
+            if (!kSlabs && di != nullptr) {
                 const uint4 *s4 = reinterpret_cast<const uint4 *>(src);
                 uint4 *d4 = reinterpret_cast<uint4 *>(di + (64 * map + ch0) * plane);
                 for (int i = threadIdx.x; i < vec; i += kTsThreads) d4[i] = s4[i];
             }
         }
+        uint2 *gslab = nullptr;
+        if constexpr (kSlabs)
+            gslab = a.slabs + (n * 16 + 8 * map + ch0 / 8) * static_cast<int64_t>(positions) * 2 + ((ch0 / 4) & 1);
         // Stage the slab (zero ring), kTsStage positions per thread in flight.
         int spy = py_first, spx = px_first;  // padded row/column of this thread's next position
         for (int pos0 = threadIdx.x; pos0 < positions; pos0 += kTsThreads * kTsStage) {
@@ -242,8 +250,10 @@ __global__ void __launch_bounds__(kTsThreads) temporal_prepare_staged_kernel(con
             for (int u = 0; u < kTsStage; ++u) {
                 const int pos = pos0 + u * kTsThreads;
                 if (pos >= positions) break;
-                slab_s[pos] = make_uint2(hv[u][0] | (static_cast<uint32_t>(hv[u][1]) << 16),
-                                         hv[u][2] | (static_cast<uint32_t>(hv[u][3]) << 16));
+                const uint2 v = make_uint2(hv[u][0] | (static_cast<uint32_t>(hv[u][1]) << 16),
+                                           hv[u][2] | (static_cast<uint32_t>(hv[u][3]) << 16));
+                slab_s[pos] = v;
+                if constexpr (kSlabs) gslab[2 * pos] = v;
             }
         }
         __syncthreads();
@@ -340,21 +350,25 @@ size_t temporal_staged_smem(int height, int width) {
 // The staged kernel's opt-in to more than 48 KB of dynamic shared memory, a per-device (and
 // per-context) function attribute.
 cudaError_t temporal_prepare_device() {
-    return cudaFuncSetAttribute(temporal_prepare_staged_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    const cudaError_t e = cudaFuncSetAttribute(temporal_prepare_staged_kernel<false>,
+                                               cudaFuncAttributeMaxDynamicSharedMemorySize, 110 * 1024);
+    if (e != cudaSuccess) return e;
+    return cudaFuncSetAttribute(temporal_prepare_staged_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                 110 * 1024);
 }
 
 cudaError_t launch_temporal_prepare(int n, int height, int width, const __half *feat_prop, const __half *feat_current,
                                     const __half *feat_n2, const __half *flow1, const __half *previous,
                                     bool has_second_order, __half *conditions, __half *deform_input, __half *flow2,
-                                    cudaStream_t stream) {
+                                    void *slabs, cudaStream_t stream) {
     TemporalArgs a{feat_prop, feat_current, feat_n2, flow1, previous, conditions, deform_input, flow2,
-                   n, height, width, has_second_order ? 1 : 0};
+                   static_cast<uint2 *>(slabs), n, height, width, has_second_order ? 1 : 0};
     const size_t smem = temporal_staged_smem(height, width);
     const bool vec_ok = (static_cast<int64_t>(height) * width) % 2 == 0 &&
                         ((reinterpret_cast<uintptr_t>(feat_prop) | reinterpret_cast<uintptr_t>(feat_current) |
                           reinterpret_cast<uintptr_t>(feat_n2) | reinterpret_cast<uintptr_t>(conditions) |
                           reinterpret_cast<uintptr_t>(deform_input)) & 15u) == 0;
+    if (slabs != nullptr && (smem == 0 || !vec_ok || deform_input != nullptr)) return cudaErrorInvalidValue;
     if (smem > 0 && vec_ok) {
         // The shared-memory opt-in was made by temporal_prepare_device, which the C entry's device
         // set-up (current_device in dcn_api.cu) runs once per device and context.
@@ -366,7 +380,10 @@ cudaError_t launch_temporal_prepare(int n, int height, int width, const __half *
         const int64_t blocks = static_cast<int64_t>(n) * 2 * kTsSlices;
         const unsigned grid =
             static_cast<unsigned>(blocks < 65535LL * 2 * kTsSlices ? blocks : 65535LL * 2 * kTsSlices);
-        return launch_dependent(temporal_prepare_staged_kernel, dim3(grid), dim3(kTsThreads), smem, stream, a);
+        if (slabs != nullptr)
+            return launch_dependent(temporal_prepare_staged_kernel<true>, dim3(grid), dim3(kTsThreads), smem, stream,
+                                    a);
+        return launch_dependent(temporal_prepare_staged_kernel<false>, dim3(grid), dim3(kTsThreads), smem, stream, a);
     }
     const int64_t plane = static_cast<int64_t>(height) * width;
     const dim3 grid(static_cast<unsigned>((plane + kTpThreads - 1) / kTpThreads), kTpSlices,

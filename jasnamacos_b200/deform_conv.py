@@ -474,6 +474,21 @@ class CudaDeformConv:
         raise_for_status(st, "dcn_forward_f16_raw")
         return out
 
+    def forward_f16_raw_grouped(self, shape, workspace, raw, flow1, flow2, packed_weight, bias, out=None, flag=None,
+                                stream=None):
+        """The raw form (offset transform fused) on an input already in the grouped layout at the
+        start of `workspace` (from regroup_input or temporal_prepare_slabs): forward_f16_raw
+        without its pre-pass."""
+        torch = _torch()
+        if out is None:
+            out = torch.empty(shape.output_count, dtype=torch.float16, device=raw.device)
+        self._check_device(workspace, raw, flow1, flow2, packed_weight, bias, out, flag)
+        st = self.lib.dcn_forward_f16_raw_grouped(
+            ctypes.byref(shape.to_c()), _ptr(workspace), _ptr(raw), _ptr(flow1), _ptr(flow2), _ptr(packed_weight),
+            _ptr(bias), _ptr(out), _ptr(flag), workspace.numel() * workspace.element_size(), _stream_handle(stream))
+        raise_for_status(st, "dcn_forward_f16_raw_grouped")
+        return out
+
     def flag_non_finite(self, values, flag, stream=None):
         """flag_non_finite_fp16 (MetalShader.swift:454-463)."""
         self._check_device(values, flag)
@@ -525,6 +540,43 @@ class CudaDeformConv:
                                                _ptr(flow2), _stream_handle(stream))
         raise_for_status(st, "dcn_temporal_prepare_f16")
         return conditions, deform_input, flow2
+
+    def temporal_slabs_bytes(self, width: int, height: int, batch: int = 1) -> int:
+        """Bytes of the deform input in the DCN's slab layout (0: the frame does not take that form)."""
+        return int(self.lib.dcn_temporal_slabs_bytes(batch, width, height))
+
+    def temporal_prepare_slabs(self, width: int, height: int, feat_prop, feat_current, feat_n2, flow1,
+                               previous_flow, has_second_order: bool, batch: int = 1, workspace=None,
+                               conditions=None, flow2=None, stream=None):
+        """temporal_prepare with the deform input written in the DCN's slab layout at the start of
+        `workspace` (dcn_temporal_prepare_slabs_f16); by default a new workspace of the size the DCN
+        of DeformConvShape.jasna_propagation(batch, height, width) takes, which forward_f16_grouped
+        and forward_f16_raw_grouped then read without a pre-pass.  Returns (conditions, workspace,
+        flow2).  Raises Unsupported for frames the slab form does not take."""
+        torch = _torch()
+        plane = width * height
+        if width <= 0 or height <= 0 or batch <= 0:
+            raise InvalidShape()
+        for t, ch in ((feat_prop, 64), (feat_current, 64), (feat_n2, 64), (flow1, 2), (previous_flow, 2)):
+            if t.numel() != batch * ch * plane:
+                raise InvalidShape()
+        dev = feat_prop.device
+        if workspace is None:
+            need = max(self.temporal_slabs_bytes(width, height, batch),
+                       self.workspace_bytes(DeformConvShape.jasna_propagation(batch, height, width)))
+            workspace = torch.empty(need, dtype=torch.uint8, device=dev)
+        if conditions is None:
+            conditions = torch.empty(batch * 196 * plane, dtype=torch.float16, device=dev)
+        if flow2 is None:
+            flow2 = torch.empty(batch * 2 * plane, dtype=torch.float16, device=dev)
+        tensors = [feat_prop, feat_current, feat_n2, flow1, previous_flow, conditions, flow2, workspace]
+        self._check_device(*tensors)
+        st = self.lib.dcn_temporal_prepare_slabs_f16(batch, width, height, *[_ptr(t) for t in tensors[:5]],
+                                                     1 if has_second_order else 0, _ptr(conditions), _ptr(flow2),
+                                                     _ptr(workspace), workspace.numel() * workspace.element_size(),
+                                                     _stream_handle(stream))
+        raise_for_status(st, "dcn_temporal_prepare_slabs_f16")
+        return conditions, workspace, flow2
 
     def device_error(self) -> None:
         """Raises DeviceTimeout if a kernel's bounded device-side wait expired since the last check."""

@@ -218,3 +218,41 @@ def test_temporal_prepare_argument_checks(lib):
     assert call(1, 64, 64, args(), cond=None) == _native.DCN_ERR_INVALID_ARGUMENT
     assert call(1, 64, 64, args(), f2=None) == _native.DCN_ERR_INVALID_ARGUMENT
     assert call(1, 64, 64, args(), di=odd) == _native.DCN_ERR_INVALID_ARGUMENT
+
+
+def test_temporal_slab_form_argument_checks(lib):
+    """dcn_temporal_prepare_slabs_f16 and dcn_forward_f16_raw_grouped reject bad extents, frames
+    the slab form does not take, missing or misaligned tensors and a short workspace before they
+    touch a device; dcn_temporal_slabs_bytes is the [batch][16][H+2][W+2] x 16-byte slab size."""
+    assert lib.dcn_temporal_slabs_bytes(2, 64, 64) == 2 * 16 * 66 * 66 * 16
+    assert lib.dcn_temporal_slabs_bytes(1, 480, 270) == 0      # too large for the shared-memory form
+    assert lib.dcn_temporal_slabs_bytes(0, 64, 64) == 0
+    p = ctypes.c_void_p(256)
+    odd = ctypes.c_void_p(264)  # 8-byte aligned only
+    full = 2 * 16 * 66 * 66 * 16
+    args = lambda **k: [k.get(n, p) for n in ("prop", "cur", "n2", "f1", "prev")]  # noqa: E731
+    call = lambda b, w, h, ins, cond=p, f2=p, ws=p, nbytes=full: lib.dcn_temporal_prepare_slabs_f16(  # noqa: E731
+        b, w, h, *ins, 1, cond, f2, ws, nbytes, None)
+    assert call(0, 64, 64, args()) == _native.DCN_ERR_INVALID_SHAPE
+    assert call(2, 64, -1, args()) == _native.DCN_ERR_INVALID_SHAPE
+    assert call(1, 480, 270, args()) == _native.DCN_ERR_UNSUPPORTED
+    assert call(1, 17, 13, args()) == _native.DCN_ERR_UNSUPPORTED   # odd pixel count
+    assert call(2, 64, 64, args(prop=odd)) == _native.DCN_ERR_INVALID_ARGUMENT
+    assert call(2, 64, 64, args(f1=None)) == _native.DCN_ERR_INVALID_ARGUMENT
+    assert call(2, 64, 64, args(), cond=odd) == _native.DCN_ERR_INVALID_ARGUMENT
+    assert call(2, 64, 64, args(), ws=None) == _native.DCN_ERR_INVALID_ARGUMENT
+    assert call(2, 64, 64, args(), ws=odd) == _native.DCN_ERR_INVALID_ARGUMENT
+    assert call(2, 64, 64, args(), nbytes=full - 1) == _native.DCN_ERR_INVALID_ARGUMENT
+
+    s = DeformConvShape.jasna_propagation(2, 64, 64).to_c()
+    need = lib.dcn_forward_f16_raw_workspace_bytes(ctypes.byref(s))
+    assert need >= full
+    raw_call = lambda ws=p, raw=p, nbytes=need, shape=s: lib.dcn_forward_f16_raw_grouped(  # noqa: E731
+        ctypes.byref(shape), ws, raw, p, p, p, p, p, None, nbytes, None)
+    bad = DeformConvShape.jasna_propagation(2, 64, 64).to_c()
+    bad.batch = 0
+    assert raw_call(shape=bad) == _native.DCN_ERR_INVALID_SHAPE
+    assert raw_call(raw=None) == _native.DCN_ERR_INVALID_ARGUMENT
+    assert raw_call(raw=odd) == _native.DCN_ERR_INVALID_ARGUMENT
+    assert raw_call(ws=None) == _native.DCN_ERR_INVALID_ARGUMENT
+    assert raw_call(nbytes=need - 1) == _native.DCN_ERR_INVALID_ARGUMENT

@@ -7,7 +7,8 @@ output must equal the oracle's bit for bit: on the reference CLI's own 3x3 case
 (JasnaCLI.swift:227-316, also under its 0.004 gate), on the 64x64 frames of the reference's
 temporal probe (TemporalPreparationProbe.swift:14-101: its feature formula, its repeat and
 first-order-zero checks), batched, with and without the deform-input copy, and on a 270x480
-frame whose flows leave the frame on every side.
+frame whose flows leave the frame on every side.  The slab form (dcn_temporal_prepare_slabs_f16)
+writes the deform input in the DCN's own layout, which the DCN then reads without its pre-pass.
 """
 
 from __future__ import annotations
@@ -199,3 +200,88 @@ def test_verify_temporal_preparation_probe(cuda_op):
     bad[123] = np.nan
     with pytest.raises(CommandFailed):
         cuda_op.verify_temporal_preparation(bad, forward)
+
+
+@pytest.mark.parametrize("w,h,frames", [(64, 64, 1), (48, 32, 2), (64, 64, 40)],
+                         ids=["64x64x1_split4", "48x32x2_split4", "64x64x40"])
+def test_slab_form_feeds_the_dcn_without_a_prepass(cuda_op, w, h, frames):
+    """dcn_temporal_prepare_slabs_f16 writes the deform input straight into the DCN's slab layout:
+    into a workspace filled with 0xA5 first, its slab bytes (zero ring included) equal what
+    dcn_regroup_input_f16 makes of the NCHW deform input, its conditions and flow2 equal
+    dcn_temporal_prepare_f16's (which match the oracle bit for bit), and the DCN reading those
+    slabs without a pre-pass (dcn_forward_f16_raw_grouped, dcn_forward_f16_grouped) gives the
+    same bits as the DCN regrouping the NCHW deform input itself.  Small batches take the
+    group-split form, whose partial sums follow the slabs in the same workspace."""
+    import torch
+
+    from jasnamacos_b200 import _native, synthetic
+    from jasnamacos_b200.deform_conv import DeformConvShape
+
+    plane = w * h
+    g = np.random.default_rng(w * 100 + h + frames)
+    f16 = lambda a: a.astype(np.float16).astype(np.float32)  # noqa: E731
+    dev = lambda a: torch.from_numpy(a.astype(np.float16)).cuda()  # noqa: E731
+    prop, cur, n2 = (f16(g.standard_normal(frames * 64 * plane)) for _ in range(3))
+    f1, prev = _flows(frames * plane, 12.0, w + 1), _flows(frames * plane, 12.0, h + 2)
+    args = (w, h, dev(prop), dev(cur), dev(n2), dev(f1), dev(prev), True)
+    shape = DeformConvShape.jasna_propagation(frames, h, w)
+    assert cuda_op.path(shape) == _native.DCN_PATH_SLAB_TC
+    cond, di, flow2 = cuda_op.temporal_prepare(*args, batch=frames)
+    ref_ws = cuda_op.regroup_input(shape, di)
+    ws = torch.full((cuda_op.workspace_bytes(shape),), 0xA5, dtype=torch.uint8, device="cuda")
+    cond_s, ws_out, flow2_s = cuda_op.temporal_prepare_slabs(*args, batch=frames, workspace=ws)
+    torch.cuda.synchronize()
+    cuda_op.device_error()
+    n = cuda_op.temporal_slabs_bytes(w, h, frames)
+    assert ws_out is ws and n == frames * 16 * (h + 2) * (w + 2) * 16
+    assert torch.equal(cond, cond_s) and torch.equal(flow2, flow2_s)
+    assert torch.equal(ws[:n], ref_ws[:n])
+    want = oracle.temporal_prepare(w, h, prop[:64 * plane], cur[:64 * plane], n2[:64 * plane], f1[:2 * plane],
+                                   prev[:2 * plane], True)
+    assert np.array_equal(cond_s[:196 * plane].float().cpu().numpy(), want[0])
+
+    wt, b = synthetic.weights(shape, 7)
+    packed, bias = cuda_op.prepack(shape, dev(f16(wt))), dev(f16(b))
+    raw = dev(f16(g.standard_normal(frames * 432 * plane)))
+    f1_d = dev(f1)
+    flag = torch.zeros(1, dtype=torch.int32, device="cuda")
+    want_raw = cuda_op.forward_f16_raw(shape, di, raw, f1_d, flow2, packed, bias, flag=flag)
+    got_raw = cuda_op.forward_f16_raw_grouped(shape, ws, raw, f1_d, flow2_s, packed, bias, flag=flag)
+    off = torch.empty(frames * 288 * plane, dtype=torch.float16, device="cuda")
+    msk = torch.empty(frames * 144 * plane, dtype=torch.float16, device="cuda")
+    for i in range(frames):
+        cuda_op.prepare_offsets(plane, raw[i * 432 * plane:(i + 1) * 432 * plane], f1_d[i * 2 * plane:(i + 1) * 2 * plane],
+                                flow2[i * 2 * plane:(i + 1) * 2 * plane], offset=off[i * 288 * plane:(i + 1) * 288 * plane],
+                                mask=msk[i * 144 * plane:(i + 1) * 144 * plane])
+    want_off = cuda_op.forward_f16(shape, di, off, msk, packed, bias, flag=flag)
+    got_off = cuda_op.forward_f16_grouped(shape, ws, off, msk, packed, bias, flag=flag)
+    torch.cuda.synchronize()
+    cuda_op.device_error()
+    assert int(flag.item()) == 0
+    assert torch.equal(got_raw, want_raw)
+    assert torch.equal(got_off, want_off)
+    assert torch.equal(ws[:n], ref_ws[:n])  # the DCN read the slabs without changing them
+
+
+def test_slab_form_rejects_frames_it_does_not_take(cuda_op):
+    """Frames the slab form does not take (too large for the shared-memory kernel, an odd pixel
+    count) raise Unsupported, and a workspace shorter than the slabs raises InvalidArgument."""
+    import torch
+
+    from jasnamacos_b200.deform_conv import InvalidArgument, Unsupported
+
+    def inputs(w, h):
+        plane = w * h
+        z = lambda c: torch.zeros(c * plane, dtype=torch.float16, device="cuda")  # noqa: E731
+        return (w, h, z(64), z(64), z(64), z(2), z(2), True)
+
+    assert cuda_op.temporal_slabs_bytes(480, 270) == 0
+    with pytest.raises(Unsupported):
+        cuda_op.temporal_prepare_slabs(*inputs(480, 270), workspace=torch.empty(1 << 20, dtype=torch.uint8,
+                                                                                 device="cuda"))
+    with pytest.raises(Unsupported):
+        cuda_op.temporal_prepare_slabs(*inputs(17, 13), workspace=torch.empty(1 << 20, dtype=torch.uint8,
+                                                                               device="cuda"))
+    short = torch.empty(cuda_op.temporal_slabs_bytes(64, 64) - 16, dtype=torch.uint8, device="cuda")
+    with pytest.raises(InvalidArgument):
+        cuda_op.temporal_prepare_slabs(*inputs(64, 64), workspace=short)
