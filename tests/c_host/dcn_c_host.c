@@ -392,6 +392,42 @@ static void check_temporal(int frames, int w, int h, uint64_t seed) {
     CHECK(mismatches == 0, "temporal %dx%d x%d: %lld values differ from the oracle", w, h, frames,
           (long long)mismatches);
     printf("temporal preparation %dx%d x%d: bit-exact against the oracle\n", w, h, frames);
+    /* The slab form: the deform input as the DCN's slabs [frames][16][H+2][W+2][8] (zero ring),
+     * written into a buffer filled with 0xA5 first; conditions and flow2 as above. */
+    const size_t slab_bytes = dcn_temporal_slabs_bytes(frames, w, h);
+    if (slab_bytes > 0 && plane % 2 == 0) {
+        void *d_ws = NULL;
+        CUDA_OK(cudaMalloc(&d_ws, slab_bytes));
+        CUDA_OK(cudaMemset(d_ws, 0xA5, slab_bytes));
+        CUDA_OK(cudaMemset(d_cond, 0, sizeof(uint16_t) * (size_t)ncond));
+        const dcn_status rs = dcn_temporal_prepare_slabs_f16(frames, w, h, d_in[0], d_in[1], d_in[2], d_in[3],
+                                                             d_in[4], 1, d_cond, d_flow2, d_ws, slab_bytes, NULL);
+        CHECK(rs == DCN_OK, "temporal slabs %dx%d: %s", w, h, dcn_status_string(rs));
+        CUDA_OK(cudaDeviceSynchronize());
+        uint16_t *slabs = (uint16_t *)malloc(slab_bytes);
+        uint16_t *cond2 = (uint16_t *)malloc(sizeof(uint16_t) * (size_t)ncond);
+        CUDA_OK(cudaMemcpy(slabs, d_ws, slab_bytes, cudaMemcpyDeviceToHost));
+        CUDA_OK(cudaMemcpy(cond2, d_cond, sizeof(uint16_t) * (size_t)ncond, cudaMemcpyDeviceToHost));
+        int64_t bad = memcmp(cond2, cond, sizeof(uint16_t) * (size_t)ncond) != 0;
+        const int sw = w + 2, sh = h + 2;
+        for (int f = 0; f < frames; ++f)
+            for (int g = 0; g < 16; ++g)
+                for (int py = 0; py < sh; ++py)
+                    for (int px = 0; px < sw; ++px)
+                        for (int c = 0; c < 8; ++c) {
+                            const int y = py - 1, x = px - 1;
+                            const int inside = y >= 0 && y < h && x >= 0 && x < w;
+                            /* di was checked against the oracle above */
+                            const uint16_t want = inside ? di[f * 128 * plane + (8 * g + c) * plane + y * w + x] : 0;
+                            bad += slabs[((((int64_t)f * 16 + g) * sh + py) * sw + px) * 8 + c] != want;
+                        }
+        CHECK(bad == 0, "temporal slabs %dx%d x%d: %lld values differ", w, h, frames, (long long)bad);
+        printf("temporal preparation %dx%d x%d, slab form: the DCN's slab layout of the oracle's deform input\n", w,
+               h, frames);
+        free(slabs);
+        free(cond2);
+        cudaFree(d_ws);
+    }
     for (int t = 0; t < 5; ++t) {
         free(in[t]);
         free(bits[t]);
