@@ -222,8 +222,8 @@ cudaError_t launch_dependent(void (*kernel)(KArgs...), dim3 grid, dim3 block, si
 // ---- offset producer of the raw-input form ---------------------------------------
 // prepare_dcn_offsets_fp16 (Sources/JasnaMetalPoC/MetalShader.swift:817-839) as the
 // tensor-core kernels evaluate it inside their producers: offset = 10*tanh(residue) + flow,
-// mask = sigmoid(logit), each rounded to FP16 like the reference's intermediate tensors and
-// returned widened to FP32.  Hardware tanh.approx.f32 (~2^-11 relative error), __expf and a
+// mask = sigmoid(logit), each rounded to FP16 like the reference's intermediate tensors (the
+// offset returned widened to FP32, the mask as FP16, the type the producers keep it in).  Hardware tanh.approx.f32 (~2^-11 relative error), __expf and a
 // fast reciprocal; both tensor-core kernels call these, so they produce the same bits.
 __device__ __forceinline__ float tanh_approx(float x) {
     float y;
@@ -235,8 +235,8 @@ __device__ __forceinline__ float raw_offset(float residue, float flow) {
     return __half2float(__float2half_rn(10.0f * tanh_approx(residue) + flow));
 }
 
-__device__ __forceinline__ float raw_mask(float logit) {
-    return __half2float(__float2half_rn(__fdividef(1.0f, 1.0f + __expf(-logit))));
+__device__ __forceinline__ __half raw_mask(float logit) {
+    return __float2half_rn(__fdividef(1.0f, 1.0f + __expf(-logit)));
 }
 
 // 32-byte read-only global load (sm_100: 256-bit vector load); `p` must be

@@ -365,7 +365,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                         const bool second = info.w == 2;
                         off_y = raw_offset(off_y, second ? pf_f2y : pf_f1y);
                         off_x = raw_offset(off_x, second ? pf_f2x : pf_f1x);
-                        mk = __float2half_rn(raw_mask(__half2float(mk)));
+                        mk = raw_mask(__half2float(mk));
                     }
                     const float y = static_cast<float>(base_y + info.y) + off_y;
                     const float x = static_cast<float>(base_x + info.z) + off_x;

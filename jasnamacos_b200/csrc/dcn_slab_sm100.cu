@@ -457,7 +457,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                         if (FromRaw) {
                             off_y = raw_offset(off_y, __half2float(s.flow[st][1][r]));
                             off_x = raw_offset(off_x, __half2float(s.flow[st][0][r]));
-                            mk = __float2half_rn(raw_mask(__half2float(mk)));
+                            mk = raw_mask(__half2float(mk));
                         }
                         const float y = (bfy[t] + tyf) + off_y;
                         const float x = (bfx[t] + txf[i]) + off_x;
