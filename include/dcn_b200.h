@@ -248,6 +248,15 @@ dcn_status dcn_forward_f16_grouped(const dcn_shape *shape, void *input_grouped,
                                    const void *bias, void *output, uint32_t *nonfinite_flag,
                                    dcn_stream stream);
 
+/* dcn_regroup_input_nhwc_f16: dcn_regroup_input_f16 for an input stored channels-last,
+ *   [N][H][W][C] FP16 (16-byte aligned; the reference's tensors are NCHW,
+ *   DeformConv.swift:110-132).  It writes the same bytes at the start of the workspace, so
+ *   dcn_forward_f16_grouped or dcn_forward_f16_raw_grouped follows unchanged.  Tensor-core
+ *   paths only (DCN_ERR_UNSUPPORTED for DCN_PATH_DIRECT shapes); workspace 16-byte aligned and
+ *   at least dcn_forward_f16_workspace_bytes(shape). */
+dcn_status dcn_regroup_input_nhwc_f16(const dcn_shape *shape, const void *input_nhwc, void *workspace,
+                                      size_t workspace_bytes, dcn_stream stream);
+
 /* ---- FP16 operator on host buffers ----------------------------------------------
  * Replaces the reference's host-array contract: MetalDeformConv.runFloat32 takes Swift
  * arrays and returns a new array (MetalRunner.swift:159-185), copying the inputs into fresh

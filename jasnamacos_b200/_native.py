@@ -122,6 +122,7 @@ PROTOTYPES = {
     ),
     "dcn_regroup_input_f16": (ctypes.c_int, [_SHAPE, _P, _P, ctypes.c_size_t, _P]),
     "dcn_forward_f16_grouped": (ctypes.c_int, [_SHAPE, _P, _P, _P, _P, _P, _P, _P, _P]),
+    "dcn_regroup_input_nhwc_f16": (ctypes.c_int, [_SHAPE, _P, _P, ctypes.c_size_t, _P]),
     "dcn_forward_f16_raw_workspace_bytes": (ctypes.c_size_t, [_SHAPE]),
     "dcn_forward_f16_raw": (
         ctypes.c_int,

@@ -33,6 +33,7 @@ SOURCES = [
     "dcn_static_scratch.cu",
     "dcn_host.cu",
     "dcn_temporal.cu",
+    "dcn_nhwc.cu",
 ]
 HEADERS = ["dcn_common.cuh"]
 

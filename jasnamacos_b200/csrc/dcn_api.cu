@@ -70,6 +70,8 @@ cudaError_t launch_temporal_prepare(int n, int height, int width, const __half *
                                     bool has_second_order, __half *conditions, __half *deform_input, __half *flow2,
                                     void *slabs, cudaStream_t stream);
 size_t temporal_staged_smem(int height, int width);
+cudaError_t launch_regroup_nhwc(bool slabs, int N, int G, int H, int W, const __half *in, void *workspace,
+                                cudaStream_t stream);
 
 uint64_t current_context_id() {
     static PFN_cuCtxGetCurrent_v4000 get_current = nullptr;
@@ -490,6 +492,23 @@ dcn_status dcn_regroup_input_f16(const dcn_shape *shape, const void *input, void
     if ((st = current_device(&dev)) != DCN_OK) return st;
     const SplitInput<__half> in{static_cast<const __half *>(input), nullptr, p.C, p.C};
     return from_cuda(launch_regroup(path, p, in, workspace, reinterpret_cast<cudaStream_t>(stream)));
+}
+
+dcn_status dcn_regroup_input_nhwc_f16(const dcn_shape *shape, const void *input_nhwc, void *workspace,
+                                      size_t workspace_bytes, dcn_stream stream) {
+    dcn_status st = validate(shape);
+    if (st != DCN_OK) return st;
+    const Params p = make_params(*shape);
+    const dcn_path path = select_path(p);
+    if (path == DCN_PATH_DIRECT) return DCN_ERR_UNSUPPORTED;
+    if (!input_nhwc || !workspace || !aligned(input_nhwc, 16) || !aligned(workspace, 16) ||
+        workspace_bytes < dcn_forward_f16_workspace_bytes(shape))
+        return DCN_ERR_INVALID_ARGUMENT;
+    DeviceInfo *dev = nullptr;
+    if ((st = current_device(&dev)) != DCN_OK) return st;
+    return from_cuda(launch_regroup_nhwc(path == DCN_PATH_SLAB_TC, p.N, p.OG, p.H, p.W,
+                                         static_cast<const __half *>(input_nhwc), workspace,
+                                         reinterpret_cast<cudaStream_t>(stream)));
 }
 
 dcn_status dcn_forward_f16_grouped(const dcn_shape *shape, void *input_grouped, const void *offset,

@@ -426,6 +426,22 @@ class CudaDeformConv:
         raise_for_status(st, "dcn_regroup_input_f16")
         return workspace
 
+    def regroup_input_nhwc(self, shape, input_nhwc, workspace=None, stream=None):
+        """regroup_input for a channels-last input [N][H][W][C] FP16 (dcn_regroup_input_nhwc_f16):
+        the same grouped bytes at the start of the workspace."""
+        torch = _torch()
+        ws_bytes = self.workspace_bytes(shape)
+        if ws_bytes == 0:
+            raise Unsupported("shape does not take a tensor-core path")
+        if workspace is None:
+            workspace = torch.empty(ws_bytes, dtype=torch.uint8, device=input_nhwc.device)
+        self._check_device(input_nhwc, workspace)
+        st = self.lib.dcn_regroup_input_nhwc_f16(ctypes.byref(shape.to_c()), _ptr(input_nhwc), _ptr(workspace),
+                                                 workspace.numel() * workspace.element_size(),
+                                                 _stream_handle(stream))
+        raise_for_status(st, "dcn_regroup_input_nhwc_f16")
+        return workspace
+
     def forward_f16_grouped(self, shape, input_grouped, offset, mask, packed_weight, bias, out=None, flag=None,
                             stream=None):
         """The fused gather + tcgen05 kernel alone, on an input already in the grouped layout."""

@@ -256,3 +256,20 @@ def test_temporal_slab_form_argument_checks(lib):
     assert raw_call(raw=odd) == _native.DCN_ERR_INVALID_ARGUMENT
     assert raw_call(ws=None) == _native.DCN_ERR_INVALID_ARGUMENT
     assert raw_call(nbytes=need - 1) == _native.DCN_ERR_INVALID_ARGUMENT
+
+
+def test_nhwc_regroup_argument_checks(lib):
+    """dcn_regroup_input_nhwc_f16 rejects direct-path shapes, missing or misaligned pointers and a
+    short workspace before it touches a device."""
+    s = DeformConvShape.jasna_propagation(2, 64, 64).to_c()
+    need = lib.dcn_forward_f16_workspace_bytes(ctypes.byref(s))
+    p = ctypes.c_void_p(256)
+    odd = ctypes.c_void_p(264)  # 8-byte aligned only
+    call = lambda x=p, ws=p, nbytes=need, shape=s: lib.dcn_regroup_input_nhwc_f16(  # noqa: E731
+        ctypes.byref(shape), x, ws, nbytes, None)
+    direct = DeformConvShape(1, 128, 64, 64, 32, 64, 64, 3, 3, 1, 1, 1, 1, 1, 1, 1, 16).to_c()
+    assert call(shape=direct) == _native.DCN_ERR_UNSUPPORTED
+    assert call(x=None) == _native.DCN_ERR_INVALID_ARGUMENT
+    assert call(x=odd) == _native.DCN_ERR_INVALID_ARGUMENT
+    assert call(ws=odd) == _native.DCN_ERR_INVALID_ARGUMENT
+    assert call(nbytes=need - 1) == _native.DCN_ERR_INVALID_ARGUMENT
