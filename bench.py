@@ -498,6 +498,56 @@ def chain_section(op, dev, w, h, frames, steps, feats, flows, cond, di, flow2, p
     return res
 
 
+def configs_section(op, dev, steps: int, peaks: dict) -> dict:
+    """Every other benchmark configuration (0-3) timed briefly on this GPU inside the default run,
+    so that each has a number from the same box and build: the same inputs, kernels and launch
+    mode as `bench.py --config C` (CUDA-graph replays for the single-image configurations, whose
+    inputs fit in L2 and stay resident, as in the reference's own repeated launches), CUDA events
+    over `steps` steps after 3 warm-up steps.  Configs 0 and 1 (one image each) are also checked
+    against the oracle; configs 2 and 3 are covered by the parity tests."""
+    import torch
+
+    from jasnamacos_b200 import _native, synthetic
+
+    res = {}
+    for c in (0, 1, 2, 3):
+        cfg = CONFIGS[c]
+        shape, first, x, off, msk, w, b = synthetic.bench_inputs(c, 0, 1, dev)
+        out = torch.empty(shape.output_count, dtype=torch.float32 if cfg["f32"] else torch.float16, device=dev)
+        flag = torch.zeros(1, dtype=torch.int32, device=dev)
+        ws = None
+        if cfg["f32"]:
+            wt, bt = torch.from_numpy(w).to(dev), torch.from_numpy(b).to(dev)
+            fn = lambda: op.forward_f32(shape, x, off, msk, wt, bt, out=out)  # noqa: E731
+            path = "direct"
+        else:
+            wt, bt = torch.from_numpy(w).to(dev).half(), torch.from_numpy(b).to(dev).half()
+            packed = op.prepack(shape, wt)
+            ws = torch.empty(max(op.workspace_bytes(shape), 16), dtype=torch.uint8, device=dev)
+            fn = lambda: op.forward_f16(shape, x, off, msk, packed, bt, out=out, flag=flag, workspace=ws)  # noqa: E731
+            path = {_native.DCN_PATH_SLAB_TC: "slab", _native.DCN_PATH_FUSED_TC: "global-gather"}.get(
+                op.path(shape), "direct")
+        step = graphed(fn, not cfg["sharded"])
+        for _ in range(3):
+            step()
+        torch.cuda.synchronize(dev)
+        ms = event_time_ms(step, steps) / steps
+        px = shape.output_pixels
+        bytes_px = 2 * BYTES_PER_PX if cfg["f32"] else BYTES_PER_PX
+        entry = {"ms_per_step": ms, "Mpx_s": px / (ms * 1e-3) / 1e6, "path": path,
+                 "frac_hbm": bytes_px * px / (ms * 1e-3) / 1e9 / peaks["hbm_gbs"],
+                 "launch": "CUDA graph replay per step" if not cfg["sharded"] else "direct launches per step",
+                 "nonfinite_flag": int(flag.item())}
+        if not cfg["f32"]:
+            entry["frac_tensor"] = FLOPS_PER_PX * px / (ms * 1e-3) / 1e12 / peaks["bf16_tflops"]
+        if c in (0, 1):
+            entry["parity"] = parity_check(c, shape, first, 1, 1, x, off, msk, out, wt, bt, None)
+        res[str(c)] = entry
+        del x, off, msk, out, ws
+    torch.cuda.empty_cache()
+    return res
+
+
 # Benchmark configurations.  Tile batches (2, 4) are sharded over the GPUs (total work
 # fixed: "strong"); single-image configurations (0, 1, 3) run one replica per GPU ("weak").
 CONFIGS = {
@@ -637,6 +687,11 @@ def run_ours(args):
     if args.config == 4 and world == 1 and not args.no_temporal:
         temporal = temporal_section(op, dev, i_end - i_begin, args.steps, peaks, dcn=(packed, b16))
         torch.cuda.empty_cache()
+
+    # ---- the other benchmark configurations, briefly, on the same GPU (default run) ---------
+    configs = None
+    if args.config == 4 and world == 1 and not args.no_configs:
+        configs = configs_section(op, dev, args.steps, peaks)
 
     # ---- final gather of every shard's output to rank 0 (N > 1) -------------------------
     # (a) serial: the timed step's output sent to rank 0 after the step (NCCL point-to-point);
@@ -876,6 +931,7 @@ def run_ours(args):
             "e2e": e2e,
             "raw_form": raw_form,
             "temporal_prepare": temporal,
+            "configs": configs,
             "gather": gather,
             "gpu_launches": launches_per_step * args.steps,
             "clocks": clocks,
@@ -907,6 +963,7 @@ def main():
     ap.add_argument("--e2e-steps", type=int, default=5)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-parity", action="store_true", help="skip the oracle check of the timed output")
+    ap.add_argument("--no-configs", action="store_true", help="skip the brief timing of configs 0-3")
     ap.add_argument("--no-temporal", action="store_true",
                     help="skip the temporal-preparation measurement (config 4, one GPU)")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
