@@ -186,7 +186,8 @@ __device__ __forceinline__ float2 pair_to_float2(uint32_t word) {
 // kSlabs: the deform input is written in the DCN's slab layout (zero ring included) straight from
 // the staging registers, in place of the NCHW copy: each block writes the 8-byte half of every
 // 16-byte position that its 4 channels make in deformable group 8 * map + ch0 / 8.
-template <bool kSlabs>
+// kQuad (frames with W % 4 == 0): interior rows are staged four pixels at a time.
+template <bool kSlabs, bool kQuad>
 __global__ void __launch_bounds__(kTsThreads) temporal_prepare_staged_kernel(const TemporalArgs a) {
     extern __shared__ __align__(16) uint8_t ts_smem[];
     // In-frame offsets are 32-bit (a staged frame holds at most a few thousand pixels); rows and
@@ -204,6 +205,7 @@ __global__ void __launch_bounds__(kTsThreads) temporal_prepare_staged_kernel(con
     const int pstep_y = kTsThreads / sw, pstep_x = kTsThreads % sw;       // padded-position stride
     const int y_first = static_cast<int>(threadIdx.x) / W, x_first = static_cast<int>(threadIdx.x) % W;
     const int py_first = static_cast<int>(threadIdx.x) / sw, px_first = static_cast<int>(threadIdx.x) % sw;
+    const int quads = kQuad ? W / 4 : 1;  // quad staging: first item and stride as (rows, quads)
     for (int64_t n = blockIdx.x / (2 * kTsSlices); n < a.N; n += gridDim.x / (2 * kTsSlices)) {
         const int64_t feat = (n * kTpChannels + ch0) * plane;
         const __half *src = (map ? a.feat_n2 : a.feat_prop) + feat;
@@ -227,33 +229,76 @@ __global__ void __launch_bounds__(kTsThreads) temporal_prepare_staged_kernel(con
         uint2 *gslab = nullptr;
         if constexpr (kSlabs)
             gslab = a.slabs + (n * 16 + 8 * map + ch0 / 8) * static_cast<int64_t>(positions) * 2 + ((ch0 / 4) & 1);
-        // Stage the slab (zero ring), kTsStage positions per thread in flight.
-        int spy = py_first, spx = px_first;  // padded row/column of this thread's next position
-        for (int pos0 = threadIdx.x; pos0 < positions; pos0 += kTsThreads * kTsStage) {
-            unsigned short hv[kTsStage][kTsSlice];
+        // Stage the slab (zero ring).
+        if constexpr (kQuad) {
+            // Interior rows four pixels at a time: one 8-byte load per channel plane (pixels
+            // 4j..4j+3 of one row; W % 4 == 0 keeps it 8-byte aligned), transposed in registers into
+            // four 8-byte positions.  The zero ring separately.
+            const int items = H * quads;
+            const int qstep_y = kTsThreads / quads, qstep_x = kTsThreads % quads;
+            int iy = static_cast<int>(threadIdx.x) / quads, ij = static_cast<int>(threadIdx.x) % quads;
+#pragma unroll 1
+            for (int t = threadIdx.x; t < items; t += kTsThreads) {
+                const int e = iy * W + 4 * ij;
+                uint2 v[kTsSlice];
 #pragma unroll
-            for (int u = 0; u < kTsStage; ++u) {
-                const int pos = pos0 + u * kTsThreads;
-                const int y = spy - 1, x = spx - 1;
-                const bool inside = pos < positions && y >= 0 && y < H && x >= 0 && x < W;
-                const int q = inside ? y * W + x : 0;
+                for (int k = 0; k < kTsSlice; ++k) v[k] = *reinterpret_cast<const uint2 *>(src + k * plane + e);
+                const int pos = (iy + 1) * sw + 4 * ij + 1;
 #pragma unroll
-                for (int k = 0; k < kTsSlice; ++k) hv[u][k] = inside ? __half_as_ushort(src[k * plane + q]) : 0;
-                spy += pstep_y;
-                spx += pstep_x;
-                if (spx >= sw) {
-                    spx -= sw;
-                    ++spy;
+                for (int i = 0; i < 4; ++i) {
+                    // position i: channels (0, 1) and (2, 3) of pixel 4j + i
+                    const uint32_t sel = (i & 1) ? 0x7632u : 0x5410u;
+                    const int w = i >> 1;
+                    const uint2 o = make_uint2(__byte_perm(w ? v[0].y : v[0].x, w ? v[1].y : v[1].x, sel),
+                                               __byte_perm(w ? v[2].y : v[2].x, w ? v[3].y : v[3].x, sel));
+                    slab_s[pos + i] = o;
+                    if constexpr (kSlabs) gslab[2 * (pos + i)] = o;
+                }
+                iy += qstep_y;
+                ij += qstep_x;
+                if (ij >= quads) {
+                    ij -= quads;
+                    ++iy;
                 }
             }
+            // The ring: rows 0 and H+1, then columns 0 and W+1 of rows 1..H.
+            const int ring = 2 * sw + 2 * H;
+#pragma unroll 1
+            for (int r = threadIdx.x; r < ring; r += kTsThreads) {
+                const int rr = r - 2 * sw;
+                const int q = r < sw ? r : r < 2 * sw ? (H + 1) * sw + (r - sw) : (rr / 2 + 1) * sw + ((rr & 1) ? W + 1 : 0);
+                slab_s[q] = make_uint2(0u, 0u);
+                if constexpr (kSlabs) gslab[2 * q] = make_uint2(0u, 0u);
+            }
+        } else {
+            // Any width: kTsStage positions per thread in flight, one 2-byte load per channel.
+            int spy = py_first, spx = px_first;  // padded row/column of this thread's next position
+            for (int pos0 = threadIdx.x; pos0 < positions; pos0 += kTsThreads * kTsStage) {
+                unsigned short hv[kTsStage][kTsSlice];
 #pragma unroll
-            for (int u = 0; u < kTsStage; ++u) {
-                const int pos = pos0 + u * kTsThreads;
-                if (pos >= positions) break;
-                const uint2 v = make_uint2(hv[u][0] | (static_cast<uint32_t>(hv[u][1]) << 16),
-                                           hv[u][2] | (static_cast<uint32_t>(hv[u][3]) << 16));
-                slab_s[pos] = v;
-                if constexpr (kSlabs) gslab[2 * pos] = v;
+                for (int u = 0; u < kTsStage; ++u) {
+                    const int pos = pos0 + u * kTsThreads;
+                    const int y = spy - 1, x = spx - 1;
+                    const bool inside = pos < positions && y >= 0 && y < H && x >= 0 && x < W;
+                    const int q = inside ? y * W + x : 0;
+#pragma unroll
+                    for (int k = 0; k < kTsSlice; ++k) hv[u][k] = inside ? __half_as_ushort(src[k * plane + q]) : 0;
+                    spy += pstep_y;
+                    spx += pstep_x;
+                    if (spx >= sw) {
+                        spx -= sw;
+                        ++spy;
+                    }
+                }
+#pragma unroll
+                for (int u = 0; u < kTsStage; ++u) {
+                    const int pos = pos0 + u * kTsThreads;
+                    if (pos >= positions) break;
+                    const uint2 v = make_uint2(hv[u][0] | (static_cast<uint32_t>(hv[u][1]) << 16),
+                                               hv[u][2] | (static_cast<uint32_t>(hv[u][3]) << 16));
+                    slab_s[pos] = v;
+                    if constexpr (kSlabs) gslab[2 * pos] = v;
+                }
             }
         }
         __syncthreads();
@@ -350,11 +395,15 @@ size_t temporal_staged_smem(int height, int width) {
 // The staged kernel's opt-in to more than 48 KB of dynamic shared memory, a per-device (and
 // per-context) function attribute.
 cudaError_t temporal_prepare_device() {
-    const cudaError_t e = cudaFuncSetAttribute(temporal_prepare_staged_kernel<false>,
-                                               cudaFuncAttributeMaxDynamicSharedMemorySize, 110 * 1024);
-    if (e != cudaSuccess) return e;
-    return cudaFuncSetAttribute(temporal_prepare_staged_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                110 * 1024);
+    const void *kernels[] = {reinterpret_cast<const void *>(temporal_prepare_staged_kernel<false, false>),
+                             reinterpret_cast<const void *>(temporal_prepare_staged_kernel<false, true>),
+                             reinterpret_cast<const void *>(temporal_prepare_staged_kernel<true, false>),
+                             reinterpret_cast<const void *>(temporal_prepare_staged_kernel<true, true>)};
+    for (const void *k : kernels) {
+        const cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, 110 * 1024);
+        if (e != cudaSuccess) return e;
+    }
+    return cudaSuccess;
 }
 
 cudaError_t launch_temporal_prepare(int n, int height, int width, const __half *feat_prop, const __half *feat_current,
@@ -380,10 +429,12 @@ cudaError_t launch_temporal_prepare(int n, int height, int width, const __half *
         const int64_t blocks = static_cast<int64_t>(n) * 2 * kTsSlices;
         const unsigned grid =
             static_cast<unsigned>(blocks < 65535LL * 2 * kTsSlices ? blocks : 65535LL * 2 * kTsSlices);
-        if (slabs != nullptr)
-            return launch_dependent(temporal_prepare_staged_kernel<true>, dim3(grid), dim3(kTsThreads), smem, stream,
-                                    a);
-        return launch_dependent(temporal_prepare_staged_kernel<false>, dim3(grid), dim3(kTsThreads), smem, stream, a);
+        const dim3 g(grid), b(kTsThreads);
+        if (width % 4 == 0)
+            return slabs != nullptr ? launch_dependent(temporal_prepare_staged_kernel<true, true>, g, b, smem, stream, a)
+                                    : launch_dependent(temporal_prepare_staged_kernel<false, true>, g, b, smem, stream, a);
+        return slabs != nullptr ? launch_dependent(temporal_prepare_staged_kernel<true, false>, g, b, smem, stream, a)
+                                : launch_dependent(temporal_prepare_staged_kernel<false, false>, g, b, smem, stream, a);
     }
     const int64_t plane = static_cast<int64_t>(height) * width;
     const dim3 grid(static_cast<unsigned>((plane + kTpThreads - 1) / kTpThreads), kTpSlices,
