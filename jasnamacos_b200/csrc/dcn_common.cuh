@@ -219,6 +219,28 @@ cudaError_t launch_dependent(void (*kernel)(KArgs...), dim3 grid, dim3 block, si
     return cudaLaunchKernelEx(&cfg, kernel, static_cast<Args &&>(args)...);
 }
 
+// launch_dependent with thread-block clusters of `cluster_x` blocks along x (the grid's x extent a
+// multiple of it).
+template <typename... KArgs, typename... Args>
+cudaError_t launch_dependent_cluster(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                                     cudaStream_t stream, unsigned cluster_x, Args &&...args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = cluster_x;
+    attr[1].val.clusterDim.y = 1;
+    attr[1].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 2;
+    return cudaLaunchKernelEx(&cfg, kernel, static_cast<Args &&>(args)...);
+}
+
 // ---- offset producer of the raw-input form ---------------------------------------
 // prepare_dcn_offsets_fp16 (Sources/JasnaMetalPoC/MetalShader.swift:817-839) as the
 // tensor-core kernels evaluate it inside their producers: offset = 10*tanh(residue) + flow,

@@ -17,6 +17,7 @@
 // the concatenation copy unnecessary.  The sampling arithmetic is the reference's (`sample_fp16`,
 // MetalShader.swift:52-74, and the CPU check's `sampleZero`, JasnaCLI.swift:213-225) with one
 // IEEE rounding per operation, so results equal the CPU restatement bit for bit.
+#include <cooperative_groups.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
@@ -38,7 +39,7 @@ struct TemporalArgs {
     __half *conditions;                                 // [N][196][H][W]
     __half *deform_input;                               // [N][128][H][W] or null
     __half *flow2;                                      // [N][2][H][W]
-    uint2 *slabs;  // the deform input as the DCN's slabs [N][16][H+2][W+2][8] (16 B per position), or null
+    uint4 *slabs;  // the deform input as the DCN's slabs [N][16][H+2][W+2][8] (16 B per position), or null
     int N, H, W;
     int has_second_order;
 };
@@ -183,9 +184,10 @@ __device__ __forceinline__ float2 pair_to_float2(uint32_t word) {
     return __half22float2(h);
 }
 
-// kSlabs: the deform input is written in the DCN's slab layout (zero ring included) straight from
-// the staging registers, in place of the NCHW copy: each block writes the 8-byte half of every
-// 16-byte position that its 4 channels make in deformable group 8 * map + ch0 / 8.
+// kSlabs: the deform input is written in the DCN's slab layout (zero ring included) from the staged
+// slices, in place of the NCHW copy.  The kernel is then launched in clusters of two blocks, the two
+// 4-channel slices of one deformable group (8 * map + ch0 / 8), which together hold whole 16-byte
+// positions.
 // kQuad (frames with W % 4 == 0): interior rows are staged four pixels at a time.
 template <bool kSlabs, bool kQuad>
 __global__ void __launch_bounds__(kTsThreads) temporal_prepare_staged_kernel(const TemporalArgs a) {
@@ -226,9 +228,6 @@ __global__ void __launch_bounds__(kTsThreads) temporal_prepare_staged_kernel(con
                 for (int i = threadIdx.x; i < vec; i += kTsThreads) d4[i] = s4[i];
             }
         }
-        uint2 *gslab = nullptr;
-        if constexpr (kSlabs)
-            gslab = a.slabs + (n * 16 + 8 * map + ch0 / 8) * static_cast<int64_t>(positions) * 2 + ((ch0 / 4) & 1);
         // Stage the slab (zero ring).
         if constexpr (kQuad) {
             // Interior rows four pixels at a time: one 8-byte load per channel plane (pixels
@@ -252,7 +251,6 @@ __global__ void __launch_bounds__(kTsThreads) temporal_prepare_staged_kernel(con
                     const uint2 o = make_uint2(__byte_perm(w ? v[0].y : v[0].x, w ? v[1].y : v[1].x, sel),
                                                __byte_perm(w ? v[2].y : v[2].x, w ? v[3].y : v[3].x, sel));
                     slab_s[pos + i] = o;
-                    if constexpr (kSlabs) gslab[2 * (pos + i)] = o;
                 }
                 iy += qstep_y;
                 ij += qstep_x;
@@ -268,7 +266,6 @@ __global__ void __launch_bounds__(kTsThreads) temporal_prepare_staged_kernel(con
                 const int rr = r - 2 * sw;
                 const int q = r < sw ? r : r < 2 * sw ? (H + 1) * sw + (r - sw) : (rr / 2 + 1) * sw + ((rr & 1) ? W + 1 : 0);
                 slab_s[q] = make_uint2(0u, 0u);
-                if constexpr (kSlabs) gslab[2 * q] = make_uint2(0u, 0u);
             }
         } else {
             // Any width: kTsStage positions per thread in flight, one 2-byte load per channel.
@@ -297,11 +294,28 @@ __global__ void __launch_bounds__(kTsThreads) temporal_prepare_staged_kernel(con
                     const uint2 v = make_uint2(hv[u][0] | (static_cast<uint32_t>(hv[u][1]) << 16),
                                                hv[u][2] | (static_cast<uint32_t>(hv[u][3]) << 16));
                     slab_s[pos] = v;
-                    if constexpr (kSlabs) gslab[2 * pos] = v;
                 }
             }
         }
-        __syncthreads();
+        if constexpr (kSlabs) {
+            // The two blocks of one deformable group (slices 2s and 2s + 1, one cluster) each write
+            // half of the group's positions as whole 16-byte slab positions: channels 0-3 from
+            // rank 0's staged slice, 4-7 from rank 1's, read through distributed shared memory.
+            namespace cg = cooperative_groups;
+            cg::cluster_group cluster = cg::this_cluster();
+            cluster.sync();  // both slices staged
+            const uint2 *lo = cluster.map_shared_rank(slab_s, 0), *hi = cluster.map_shared_rank(slab_s, 1);
+            uint4 *g = a.slabs + (n * 16 + 8 * map + ch0 / 8) * static_cast<int64_t>(positions);
+            const int half = (positions + 1) / 2;
+            const int end = cluster.block_rank() ? positions : half;
+#pragma unroll 1
+            for (int pos = (cluster.block_rank() ? half : 0) + threadIdx.x; pos < end; pos += kTsThreads) {
+                const uint2 l = lo[pos], h = hi[pos];
+                g[pos] = make_uint4(l.x, l.y, h.x, h.y);
+            }
+        } else {
+            __syncthreads();
+        }
         // Map 1 reads the second-order flow from second_order_flow_kernel, which this kernel
         // follows as a programmatic dependent: everything above ran while that kernel did.  Map 0
         // reads flow1, an input, and writes nothing that kernel writes.
@@ -349,7 +363,12 @@ __global__ void __launch_bounds__(kTsThreads) temporal_prepare_staged_kernel(con
                 ++y;
             }
         }
-        __syncthreads();  // the slab is rewritten for the next frame
+        // The slab is rewritten for the next frame (in the slab form, after the partner block has
+        // read it too).
+        if constexpr (kSlabs)
+            cooperative_groups::this_cluster().sync();
+        else
+            __syncthreads();
     }
 }
 
@@ -411,7 +430,7 @@ cudaError_t launch_temporal_prepare(int n, int height, int width, const __half *
                                     bool has_second_order, __half *conditions, __half *deform_input, __half *flow2,
                                     void *slabs, cudaStream_t stream) {
     TemporalArgs a{feat_prop, feat_current, feat_n2, flow1, previous, conditions, deform_input, flow2,
-                   static_cast<uint2 *>(slabs), n, height, width, has_second_order ? 1 : 0};
+                   static_cast<uint4 *>(slabs), n, height, width, has_second_order ? 1 : 0};
     const size_t smem = temporal_staged_smem(height, width);
     const bool vec_ok = (static_cast<int64_t>(height) * width) % 2 == 0 &&
                         ((reinterpret_cast<uintptr_t>(feat_prop) | reinterpret_cast<uintptr_t>(feat_current) |
@@ -430,11 +449,15 @@ cudaError_t launch_temporal_prepare(int n, int height, int width, const __half *
         const unsigned grid =
             static_cast<unsigned>(blocks < 65535LL * 2 * kTsSlices ? blocks : 65535LL * 2 * kTsSlices);
         const dim3 g(grid), b(kTsThreads);
+        // The grid is a whole number of frames' 32 blocks, so slices 2s and 2s + 1 of a (frame, map)
+        // are adjacent blocks and form one cluster of two.
         if (width % 4 == 0)
-            return slabs != nullptr ? launch_dependent(temporal_prepare_staged_kernel<true, true>, g, b, smem, stream, a)
-                                    : launch_dependent(temporal_prepare_staged_kernel<false, true>, g, b, smem, stream, a);
-        return slabs != nullptr ? launch_dependent(temporal_prepare_staged_kernel<true, false>, g, b, smem, stream, a)
-                                : launch_dependent(temporal_prepare_staged_kernel<false, false>, g, b, smem, stream, a);
+            return slabs != nullptr
+                       ? launch_dependent_cluster(temporal_prepare_staged_kernel<true, true>, g, b, smem, stream, 2, a)
+                       : launch_dependent(temporal_prepare_staged_kernel<false, true>, g, b, smem, stream, a);
+        return slabs != nullptr
+                   ? launch_dependent_cluster(temporal_prepare_staged_kernel<true, false>, g, b, smem, stream, 2, a)
+                   : launch_dependent(temporal_prepare_staged_kernel<false, false>, g, b, smem, stream, a);
     }
     const int64_t plane = static_cast<int64_t>(height) * width;
     const dim3 grid(static_cast<unsigned>((plane + kTpThreads - 1) / kTpThreads), kTpSlices,

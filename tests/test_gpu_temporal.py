@@ -202,8 +202,8 @@ def test_verify_temporal_preparation_probe(cuda_op):
         cuda_op.verify_temporal_preparation(bad, forward)
 
 
-@pytest.mark.parametrize("w,h,frames", [(64, 64, 1), (48, 32, 2), (64, 64, 40)],
-                         ids=["64x64x1_split4", "48x32x2_split4", "64x64x40"])
+@pytest.mark.parametrize("w,h,frames", [(64, 64, 1), (48, 32, 2), (46, 28, 3), (64, 64, 40)],
+                         ids=["64x64x1_split4", "48x32x2_split4", "46x28x3_width_not_4k", "64x64x40"])
 def test_slab_form_feeds_the_dcn_without_a_prepass(cuda_op, w, h, frames):
     """dcn_temporal_prepare_slabs_f16 writes the deform input straight into the DCN's slab layout:
     into a workspace filled with 0xA5 first, its slab bytes (zero ring included) equal what
