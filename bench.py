@@ -548,6 +548,32 @@ def configs_section(op, dev, steps: int, peaks: dict) -> dict:
     return res
 
 
+def nhwc_section(op, dev, shape, x, steps: int, peaks: dict) -> dict:
+    """The channels-last pre-pass (dcn_regroup_input_nhwc_f16) on the benchmark's own input, stored
+    [N][H][W][C]: device time (CUDA events) and HBM roofline (it reads the input once and writes the
+    grouped layout once), with its bytes compared against the NCHW pre-pass's off the timed region."""
+    import torch
+
+    x_nhwc = x.view(shape.batch, shape.input_channels, shape.input_height, shape.input_width).permute(
+        0, 2, 3, 1).contiguous().view(-1)
+    ws_ref = op.regroup_input(shape, x)
+    ws = torch.empty_like(ws_ref)
+    fn = lambda: op.regroup_input_nhwc(shape, x_nhwc, workspace=ws)  # noqa: E731
+    for _ in range(3):
+        fn()
+    torch.cuda.synchronize(dev)
+    ms = event_time_ms(fn, steps) / steps
+    grouped = op.grouped_input_bytes(shape)
+    same = bool(torch.equal(ws[:grouped], ws_ref[:grouped]))
+    moved = shape.input_count * 2 + grouped
+    del x_nhwc, ws, ws_ref
+    torch.cuda.empty_cache()
+    return {"ms": ms, "GB_s": moved / (ms * 1e-3) / 1e9, "frac_hbm": moved / (ms * 1e-3) / 1e9 / peaks["hbm_gbs"],
+            "algorithmic_bytes": moved, "bytes_equal_to_nchw_prepass": same,
+            "what": "dcn_regroup_input_nhwc_f16: the pre-pass for a channels-last input (reads the input once, "
+                    "writes the grouped layout once)"}
+
+
 # Benchmark configurations.  Tile batches (2, 4) are sharded over the GPUs (total work
 # fixed: "strong"); single-image configurations (0, 1, 3) run one replica per GPU ("weak").
 CONFIGS = {
@@ -692,6 +718,9 @@ def run_ours(args):
     configs = None
     if args.config == 4 and world == 1 and not args.no_configs:
         configs = configs_section(op, dev, args.steps, peaks)
+    nhwc = None
+    if args.config == 4 and world == 1 and not args.no_configs:
+        nhwc = nhwc_section(op, dev, shape, x, args.steps, peaks)
 
     # ---- final gather of every shard's output to rank 0 (N > 1) -------------------------
     # (a) serial: the timed step's output sent to rank 0 after the step (NCCL point-to-point);
@@ -932,6 +961,7 @@ def run_ours(args):
             "raw_form": raw_form,
             "temporal_prepare": temporal,
             "configs": configs,
+            "nhwc_prepass": nhwc,
             "gather": gather,
             "gpu_launches": launches_per_step * args.steps,
             "clocks": clocks,

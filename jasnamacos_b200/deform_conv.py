@@ -297,6 +297,17 @@ class CudaDeformConv:
     def workspace_bytes(self, shape: DeformConvShape) -> int:
         return int(self.lib.dcn_forward_f16_workspace_bytes(ctypes.byref(shape.to_c())))
 
+    def grouped_input_bytes(self, shape: DeformConvShape) -> int:
+        """Bytes of the grouped input at the start of the workspace: zero-bordered slabs on the slab
+        path, corner pairs on the global-gather path, 0 on the direct path."""
+        path = self.path(shape)
+        n, g, h, w = shape.batch, shape.offset_groups, shape.input_height, shape.input_width
+        if path == _native.DCN_PATH_SLAB_TC:
+            return n * g * (h + 2) * (w + 2) * 16
+        if path == _native.DCN_PATH_FUSED_TC:
+            return n * g * h * (w + 1) * 32
+        return 0
+
     def raw_workspace_bytes(self, shape: DeformConvShape) -> int:
         """Scratch of forward_f16_raw; 0 when the shape has no raw form (odd group count or direct path)."""
         return int(self.lib.dcn_forward_f16_raw_workspace_bytes(ctypes.byref(shape.to_c())))
