@@ -659,6 +659,76 @@ __global__ void __launch_bounds__(kBlock, kMinBlocks) regroup_slabs_x4_kernel(co
     }
 }
 
+// The same transform for large batches, with whole-sector stores.  Item (py, j < W/4) holds
+// positions py*sw + 4j + 1 .. + 4, item (py, W/4) positions py*sw + W + 1 and the next one (column
+// 0 of row py + 1), and item 0 position 0 as well, so the items of a block cover one contiguous
+// range of the slab.  Each block assembles its range in shared memory, then writes it with
+// consecutive 16-byte stores (the transposed values of one thread are 64 bytes apart otherwise,
+// and each store instruction would fill half sectors).
+template <int kBlock>
+__global__ void __launch_bounds__(kBlock) regroup_slabs_staged_kernel(const SplitInput<__half> in,
+                                                                       uint4 *__restrict__ out, int N, int H, int W) {
+    __shared__ uint4 stage[kBlock * 4 + 1];
+    allow_dependent_launch();  // the slab kernel may start its set-up
+    const int per_row = W / 4 + 1;
+    const int items = (H + 2) * per_row;
+    const int sw = W + 2;
+    const int positions = (H + 2) * sw;
+    const int g = blockIdx.y;
+    const int groups = gridDim.y;
+    const int t0 = blockIdx.x * kBlock;
+    const int t = t0 + static_cast<int>(threadIdx.x);
+    const auto first_position = [&](int it) {
+        const int r = it / per_row, c = it - r * per_row;
+        return it == 0 ? 0 : r * sw + (c < W / 4 ? 4 * c + 1 : W + 1);
+    };
+    const int p_begin = first_position(t0);
+    const int p_end = t0 + kBlock < items ? first_position(t0 + kBlock) : positions;
+    const int py = t / per_row;
+    const int j = t - py * per_row;
+    const int64_t plane = static_cast<int64_t>(H) * W;
+    const bool interior_row = py >= 1 && py <= H;
+    const uint4 zero = make_uint4(0u, 0u, 0u, 0u);
+    for (int64_t n = blockIdx.z; n < N; n += gridDim.z) {
+        if (t < items) {
+            if (j == W / 4) {
+                const int q = py * sw + W + 1 - p_begin;
+                stage[q] = zero;
+                if (py + 1 < H + 2) stage[q + 1] = zero;
+            } else {
+                uint4 o[4] = {zero, zero, zero, zero};
+                if (interior_row) {
+                    const __half *src = in.channel(n, g * 8, plane) + static_cast<int64_t>(py - 1) * W + 4 * j;
+                    uint2 v[8];
+#pragma unroll
+                    for (int c = 0; c < 8; ++c) v[c] = *reinterpret_cast<const uint2 *>(src + c * plane);
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) {
+                        const int w = i >> 1;
+                        const uint32_t sel = (i & 1) ? 0x7632u : 0x5410u;  // high or low halves
+                        uint32_t r[4];
+#pragma unroll
+                        for (int c2 = 0; c2 < 4; ++c2) {
+                            const uint32_t a = w ? v[2 * c2].y : v[2 * c2].x;
+                            const uint32_t b = w ? v[2 * c2 + 1].y : v[2 * c2 + 1].x;
+                            r[c2] = __byte_perm(a, b, sel);
+                        }
+                        o[i] = make_uint4(r[0], r[1], r[2], r[3]);
+                    }
+                }
+                const int q = py * sw + 4 * j + 1 - p_begin;
+                if (t == 0) stage[q - 1] = zero;  // position 0
+#pragma unroll
+                for (int i = 0; i < 4; ++i) stage[q + i] = o[i];
+            }
+        }
+        __syncthreads();
+        uint4 *dst = out + (n * groups + g) * positions;
+        for (int k = p_begin + static_cast<int>(threadIdx.x); k < p_end; k += kBlock) dst[k] = stage[k - p_begin];
+        __syncthreads();  // the stage is refilled for the next image
+    }
+}
+
 // Weights -> per-group SW32 K-major B blocks.  Group g, block kk (K = 16: taps 2kk,
 // 2kk+1 x 8 channels), output channel row n (0..63), 16-byte physical chunk pc:
 // logical chunk c = pc ^ ((n >> 2) & 1), tap = 2kk + c (tap 9 is zero), channel
@@ -778,8 +848,8 @@ cudaError_t launch_regroup_slabs(const Params &p, const SplitInput<__half> &inpu
                                                                              p.N, p.H, p.W);
         } else {
             const dim3 grid(static_cast<unsigned>((threads + 255) / 256), static_cast<unsigned>(p.C / 8), images);
-            slab::regroup_slabs_x4_kernel<256, 1><<<grid, 256, 0, stream>>>(input, static_cast<uint4 *>(workspace),
-                                                                            p.N, p.H, p.W);
+            slab::regroup_slabs_staged_kernel<256><<<grid, 256, 0, stream>>>(input, static_cast<uint4 *>(workspace),
+                                                                             p.N, p.H, p.W);
         }
     } else {
         const int positions = (p.H + 2) * (p.W + 2);
